@@ -1,0 +1,370 @@
+"""Batch-1 decode benchmark (the BASELINE.json metric): decode tok/s of the Mistral-7B architecture
+(fp16 weights, seeded synthetic .yalm checkpoint, 4k context) on N B200s, with the fraction of the
+HBM weight-streaming roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config mistral-7b|tiny|llama-70b]
+    python bench.py --impl reference ...     # yalm's own CPU decode path (oracle/_ref) on the host cores
+
+Workload: a 16-token random prompt (HYDRATE, last token OUTPUT_LOGITS),
+then decode steps at positions 16..135 (120 decode tokens), wrapping back to 16 for K > 120 so the
+KV length distribution stays that of the config.  One step = one decode token = one forward pass.
+
+  value  tok/s with everything resident on the device: K back-to-back yb_forward_async steps
+         (teacher-forced tokens), CUDA events on the engine stream, max over ranks.
+  e2e    the same metric through the public C-ABI call a yalm caller makes (yb_forward with a host
+         logits buffer: token id in, 128 KB of fp32 logits out to pinned host memory, greedy argmax
+         on the host picks the next token), wall clock around the K calls.
+Under torchrun (N > 1) each rank is one tensor-parallel shard (heads, kv heads, FFN hidden and
+vocabulary split N ways); partial sums cross NVLink inside the wo / w2 kernels.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT_LEN, DECODE_LEN = 16, 120
+METRIC = "batch-1 decode tok/s (Mistral-7B fp16, 4k ctx)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def model_file(config: str, rank: int, world: int, dist):
+    from yalm_b200 import synth
+    shape = synth.SHAPES[config]
+    d = synth.scratch_dir(synth.file_bytes(shape))
+    path = os.path.join(d, f"yalm_{config}_seed0.yalm")
+    if rank == 0:
+        t = time.time()
+        synth.write_yalm(path, shape, seed=0)
+        log(f"[bench] checkpoint {path} ready in {time.time() - t:.1f}s")
+    if world > 1:
+        dist.barrier()
+    return path
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            self.proc.send_signal(signal.SIGTERM)
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(path: str, context: int, n_decode: int, prompt_len: int = 2):
+    """yalm's own CPU decode path (oracle/_ref/ref_decode, built from the reference sources) on a
+    bounded sample of the same workload, all host cores."""
+    import oracle
+    if not os.path.exists(oracle.REF_BIN):
+        return None
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(99)
+    prompt = [str(int(t)) for t in rng.integers(0, 32000, prompt_len)]
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads))
+    r = subprocess.run([oracle.REF_BIN, path, str(context), str(n_decode), str(threads)] + prompt,
+                       capture_output=True, text=True, env=env, timeout=1800)
+    line = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    if r.returncode != 0 or not line:
+        log("[bench] reference CPU run failed:", r.stderr[-2000:])
+        return None
+    d = json.loads(line[-1])
+    d["threads"] = threads
+    return d
+
+
+def run_reference(args):
+    """--impl reference: yalm's CPU decode path on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from yalm_b200 import synth
+    shape = synth.SHAPES[args.config]
+    path = model_file(args.config, 0, 1, None)
+    context = 8192 if args.config == "llama-70b" else 0
+    # Each step is one full decode token of the reference; the sample is bounded to keep the run
+    # to a few minutes (the 7B CPU path takes ~0.1-0.5 s per token).
+    n = max(1, min(args.steps, args.ref_max_steps))
+    d = cpu_baseline(path, context, n + args.warmup, prompt_len=2)
+    if d is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/ref_decode missing or failed"}))
+        return 0
+    steps = d["step_s"][args.warmup:]
+    t = sum(steps)
+    v = len(steps) / t
+    sample = (f"{len(steps)} timed decode tokens (+{args.warmup} warm-up) of the full {args.config} model after a "
+              f"2-token prompt, yalm -d cpu code path (Model::forward) via oracle/_ref/ref_decode")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": len(steps), "warmup": args.warmup, "ms_per_step": round(1000 * t / len(steps), 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 weights, f32 compute",
+        "data": "synthetic (seeded N(0,0.02) fp16 weights, random token ids)",
+        "config": {"workload": f"{args.config} batch-1 decode, yalm CPU path", "model": args.config,
+                   "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_LEN, "parallelism": "cpu"},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
+                         "sample": sample},
+        "gpu_launches": 0,
+    }))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=480)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--config", default="mistral-7b", choices=["tiny", "mistral-7b", "llama-70b"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-max-steps", type=int, default=12)
+    ap.add_argument("--cpu-baseline-steps", type=int, default=6)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-profile", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    from yalm_b200 import InferenceMode, InferenceState, Model, YALMData, build, _lib
+    build.build_all()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    path = model_file(args.config, rank, world, dist)
+    context = 8192 if args.config == "llama-70b" else 0
+    y = YALMData(path)
+    t = time.time()
+    m = Model(y, context=context).cuda(local, rank, world)
+    if world > 1:
+        def ag(b):
+            out = [None] * world
+            dist.all_gather_object(out, b)
+            return out
+        m.tp_join(ag)
+    log(f"[bench] rank {rank}: engine ready in {time.time() - t:.1f}s")
+    c = m.config
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, c.vocab_size, PROMPT_LEN)
+    stream_toks = rng.integers(0, c.vocab_size, 4096)
+    s = InferenceState(c)
+    for pos, tok in enumerate(prompt):
+        m.forward(s, int(tok), pos, InferenceMode.OUTPUT_LOGITS if pos + 1 == PROMPT_LEN else InferenceMode.HYDRATE_KV_CACHE)
+
+    def pos_of(i):
+        return PROMPT_LEN + (i % DECODE_LEN)
+
+    stream = torch.cuda.ExternalStream(m.stream_ptr())
+    # ---------------------------------------------------------------- device-resident value
+    for i in range(args.warmup):
+        m.forward_async(int(stream_toks[i % 4096]), pos_of(i))
+    m.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            j = args.warmup + i
+            m.forward_async(int(stream_toks[j % 4096]), pos_of(j))
+        ev1.record(stream)
+        ev1.synchronize()
+        m.sync()
+    ms_dev = ev0.elapsed_time(ev1)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if world > 1:
+        tt = torch.tensor([ms_dev], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_dev = float(tt.item())
+    value = args.steps / (ms_dev / 1000.0)
+
+    # ---------------------------------------------------------------- end to end through the C ABI
+    logits_host = torch.empty(c.vocab_size, dtype=torch.float32, pin_memory=True)
+    lg = logits_host.numpy()
+
+    class PinnedState(InferenceState):
+        def logits(self):
+            return lg
+
+    ps = PinnedState(c)
+    for pos, tok in enumerate(prompt):
+        m.forward(ps, int(tok), pos, InferenceMode.OUTPUT_LOGITS if pos + 1 == PROMPT_LEN else InferenceMode.HYDRATE_KV_CACHE)
+    e2e_steps = args.steps
+    for i in range(args.warmup):
+        m.forward(ps, int(np.argmax(lg)), pos_of(i))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        tok = int(np.argmax(lg))  # greedy, as yalm's sampler at temperature 0 (sampler.cpp:27-38)
+        m.forward(ps, tok, pos_of(args.warmup + i))
+    t_e2e = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([t_e2e], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_e2e = float(tt.item())
+    e2e = e2e_steps / t_e2e
+
+    # ---------------------------------------------------------------- dominant kernel roofline
+    peak, peak_kind = measured_peaks()
+    kv_mean = PROMPT_LEN + (DECODE_LEN + 1) / 2.0
+    step_bytes = c.weight_bytes_per_token(world) + c.kv_bytes_per_token(int(round(kv_mean)), world) + \
+        c.n_layers * 2 * (c.n_kv_heads // world) * c.head_dim * 2
+    step_gbs = step_bytes / (ms_dev / args.steps / 1000.0) / 1e9
+    roofline = None
+    kernels = {}
+    if world == 1 and not args.no_profile:
+        names = ["qkv", "attention", "wo", "gateup", "w2", "classifier"]
+        hid, dim = c.hidden_dim, c.dim
+        q_dim, kv_dim = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
+        kbytes = {"qkv": (q_dim + 2 * kv_dim) * dim * 2 + dim * 8 + (q_dim + 2 * kv_dim) * 4,
+                  "wo": dim * q_dim * 2 + q_dim * 4 + dim * 8,
+                  "gateup": 2 * hid * dim * 2 + dim * 8 + hid * 4,
+                  "w2": dim * hid * 2 + hid * 4 + dim * 8,
+                  "classifier": c.vocab_size * dim * 2 + dim * 8 + c.vocab_size * 4}
+        import ctypes
+        for wi, nm in enumerate(names):
+            msv = ctypes.c_float()
+            _lib.call("yb_profile_kernel", m.engine, wi, c.n_layers * 4, ctypes.byref(msv))
+            kernels[nm] = {"us": round(msv.value * 1000, 2)}
+            if nm in kbytes:
+                kernels[nm]["gbs"] = round(kbytes[nm] / (msv.value / 1000) / 1e9, 1)
+        dom = "gateup"
+        achieved = kernels[dom]["gbs"]
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                traffic = json.load(f).get(f"{args.config}:{dom}")
+        except Exception:
+            traffic = None
+        roofline = {"bound": "hbm", "kernel": f"gemv gate/up (fused W1/W3 + SwiGLU, {2 * hid}x{dim} fp16)",
+                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
+                    "fallback 6650 GB/s", "traffic": traffic,
+                    "algorithmic_bytes_per_launch": kbytes[dom]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        d = cpu_baseline(path, context, args.cpu_baseline_steps)
+        if d:
+            st = d["step_s"]
+            cpu = {"value": round(len(st) / sum(st), 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
+                   "sample": f"{len(st)} decode tokens of the full {args.config} model after a 2-token prompt, yalm "
+                             f"-d cpu code path (oracle/_ref/ref_decode), {d['threads']} OpenMP threads"}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        launches_per_step = 1 + c.n_layers * (4 + m_w2_panels(m)) + 1 + (1 if world > 1 else 0)
+        out = {
+            "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_dev / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 weights, f32 accumulate/activations",
+            "data": "synthetic (seeded N(0,0.02) fp16 weights in the .yalm layout, random token ids)",
+            "config": {"workload": f"{args.config} batch-1 decode: {PROMPT_LEN}-token prompt, decode positions "
+                                   f"{PROMPT_LEN}..{PROMPT_LEN + DECODE_LEN - 1}", "model": args.config,
+                       "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_LEN, "context": c.max_seq_len,
+                       "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights streamed every step: "
+                                                          f"{step_bytes / 1e9:.2f} GB/step/rank)"},
+            "e2e": {"value": round(e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4 * c.vocab_size},
+            "roofline": roofline,
+            "step_roofline": {"bytes_per_step_per_rank": step_bytes, "achieved_gbs": round(step_gbs, 1), "peak": peak,
+                              "frac": round(step_gbs / peak, 4)},
+            "kernels_us": kernels,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "gpu_launches": launches_per_step * args.steps,
+        }
+        print(json.dumps(out))
+    m.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def m_w2_panels(m) -> int:
+    hid = m.config.hidden_dim // m.tp_size
+    p = 1
+    while hid // p > 14336 or (hid // p) % 8:
+        p += 1
+    return p
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,197 @@
+/*
+ * yalm_b200 — C ABI of the B200 (sm_100a) batch-1 decode engine for yalm .yalm checkpoints.
+ *
+ * The engine replaces the GPU side of yalm's `Model::forward` device dispatch
+ * (src/model.cpp:479-494 of the yalm repository): the CUDA-graph backend `_forward_cuda`
+ * (src/infer.cu:1274-1378) and the cooperative backend `yalm_coop_prepare` / `yalm_coop_forward`
+ * (src/coop.h:5-6).  A yalm build binds it from a small shim: the shim fills
+ * `yb_config` / `yb_weights` from yalm's `Config` and `Block` host pointers (the mmap'd .yalm
+ * tensors, before `Model::cuda()` would upload them) and calls `yb_forward` with
+ * `InferenceState::logits()`.
+ *
+ * Conventions
+ *  - Every entry point that can fail returns 0 on success or a negative YB_E* code, and never
+ *    aborts the process (yalm's CUDA_CHECK aborts, src/infer.cu:14-22).  The message of the last
+ *    failure on the calling thread is available from yb_last_error().
+ *  - All pointers in this header are host pointers unless the name says `_dev`.
+ *  - fp16 values cross the ABI as uint16_t bit patterns (yalm's f16_t, src/codec.h:13).
+ */
+#ifndef YALM_B200_H
+#define YALM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define YB_OK 0
+#define YB_E_INVALID (-1)      /* bad argument or unsupported shape */
+#define YB_E_CUDA (-2)         /* a CUDA runtime call failed */
+#define YB_E_TIMEOUT (-3)      /* a bounded device-side wait ran out (status word set) */
+#define YB_E_UNSUPPORTED (-4)  /* valid for yalm but not built here (MoE, fp32 weights) */
+
+/* InferenceMode, src/model.h:43-46 */
+#define YB_MODE_HYDRATE_KV_CACHE 0
+#define YB_MODE_OUTPUT_LOGITS 1
+
+/* Config, src/model.h:56-82 (fields the decode path uses).  act: 0 = GELU, 1 = SILU
+ * (ActivationType, src/model.h:19-22).  weight_dtype: 1 = F16 (DType order, src/codec.h:15-25);
+ * only F16 is supported.  n_experts must be 0. */
+typedef struct yb_config {
+  int dim;
+  int hidden_dim;
+  int head_dim;
+  int n_layers;
+  int n_heads;
+  int n_kv_heads;
+  int vocab_size;
+  int max_seq_len;
+  int rotary_dim;
+  int act;
+  int n_experts;
+  int weight_dtype;
+  float rope_theta;
+  float norm_eps;
+  float qkv_clip; /* FLT_MAX when the checkpoint has no qkv_clip (src/model.cpp:59) */
+} yb_config;
+
+/* Host pointers to the tensors `Model` / `Block` hold before `cuda()` (src/model.h:249-264,
+ * 276-281); per-layer arrays have n_layers entries.  Matrices are fp16 row-major exactly as in
+ * the .yalm file.  wcls may equal token_embedding_table (tied embeddings, src/model.cpp:425-434). */
+typedef struct yb_weights {
+  const uint16_t* token_embedding_table; /* [vocab_size, dim] */
+  const float* rms_final_weight;         /* [dim] */
+  const uint16_t* wcls;                  /* [vocab_size, dim] */
+  const float* const* rms_att_weight;    /* [n_layers] -> [dim] */
+  const float* const* rms_ffn_weight;    /* [n_layers] -> [dim] */
+  const uint16_t* const* wq;             /* [n_layers] -> [n_heads*head_dim, dim] */
+  const uint16_t* const* wk;             /* [n_layers] -> [n_kv_heads*head_dim, dim] */
+  const uint16_t* const* wv;             /* [n_layers] -> [n_kv_heads*head_dim, dim] */
+  const uint16_t* const* wo;             /* [n_layers] -> [dim, n_heads*head_dim] */
+  const uint16_t* const* w1;             /* [n_layers] -> [hidden_dim, dim] */
+  const uint16_t* const* w2;             /* [n_layers] -> [dim, hidden_dim] */
+  const uint16_t* const* w3;             /* [n_layers] -> [hidden_dim, dim] */
+} yb_weights;
+
+typedef struct yb_engine yb_engine;
+
+/* ---------------------------------------------------------------- engine lifecycle */
+
+/* Replaces Model::cuda() + InferenceState::cuda() (src/model.cpp:437-451, 342-361) and
+ * yalm_coop_prepare (src/coop.h:5): uploads this rank's shard of the weights to `device`,
+ * allocates the KV cache and activations, and records the per-step CUDA graphs.
+ * tp_rank / tp_size: tensor-parallel position (tp_size 1 = single GPU).  For tp_size > 1 the
+ * engines of all ranks must be joined with yb_tp_* before the first forward. */
+int yb_create(const yb_config* cfg, const yb_weights* w, int device, int tp_rank, int tp_size, yb_engine** out);
+
+/* Replaces Model::forward on a GPU device (src/model.cpp:479-494; _forward_cuda,
+ * src/infer.cu:1274-1294; yalm_coop_forward, src/coop.h:6).  Runs one decode step for `token` at
+ * position `pos` (ring buffer + attention sinks past max_seq_len, src/infer.cpp:489-494).
+ * mode YB_MODE_OUTPUT_LOGITS: returns after the step completes, with vocab_size fp32 logits in
+ * `logits` (InferenceState::logits(), any host memory).  YB_MODE_HYDRATE_KV_CACHE: only the KV
+ * cache is updated; returns without waiting for the GPU, `logits` is ignored. */
+int yb_forward(yb_engine* e, int token, int pos, int mode, float* logits);
+
+/* Same step, logits left on the device (yb_logits_dev) and no host synchronisation: for
+ * device-resident pipelines and benchmarks.  Follow with yb_sync before reading results. */
+int yb_forward_async(yb_engine* e, int token, int pos, int mode);
+int yb_sync(yb_engine* e);
+const float* yb_logits_dev(yb_engine* e);
+/* The CUDA stream the engine runs on (cudaStream_t). */
+void* yb_stream(yb_engine* e);
+
+/* Reads n cache slots [slot0, slot0 + n) of one layer / local kv head as fp16 bits in canonical
+ * [slot][head_dim] order (yalm keeps K 16-tiled, src/model.h:14-17, and V as [head_dim][slot],
+ * src/infer.cpp:304; this engine keeps both as [kv_head][slot][head_dim]). */
+int yb_read_kv(yb_engine* e, int layer, int kv_head, int slot0, int n, uint16_t* k_out, uint16_t* v_out);
+
+/* Status word the kernels of the last step wrote (0 = healthy; bit 0 TMA-stage wait timed out,
+ * bit 1 tensor-parallel peer wait timed out, bit 2 device-side argument check failed). */
+unsigned yb_status(yb_engine* e);
+int yb_clear_status(yb_engine* e);
+
+void yb_destroy(yb_engine* e);
+
+/* Diagnostics: launches one of the engine's decode kernels `iters` times back to back on its own
+ * weights and buffers (layer i mod n_layers for launch i, chained with programmatic dependent
+ * launch as inside a step) and writes the mean device time per launch, from CUDA events on the
+ * engine's stream, to *ms_per_launch.  which: 0 QKV, 1 attention, 2 wo, 3 gate/up, 4 w2,
+ * 5 classifier.  Clobbers the activations and the KV slot of the last step's position, so call it
+ * between sequences, not in the middle of one.  Single-GPU engines only. */
+int yb_profile_kernel(yb_engine* e, int which, int iters, float* ms_per_launch);
+
+/* Copies the message of the last failure on this thread into buf (NUL-terminated, truncated to
+ * n bytes); returns the full message length. */
+int yb_last_error(char* buf, int n);
+
+/* ---------------------------------------------------------------- tensor parallelism
+ * One process (or thread) per GPU.  Each rank exports an opaque blob describing its exchange
+ * buffers (CUDA IPC handles), the blobs of all ranks are exchanged by the caller (e.g. an
+ * all-gather over torch.distributed), and each rank imports all of them.  After that the engines
+ * exchange partial sums over NVLink peer memory inside the wo / w2 kernels (no NCCL call on the
+ * data path).  All ranks must then call yb_forward with identical (token, pos, mode) sequences. */
+int yb_tp_export(yb_engine* e, void* blob, size_t blob_bytes, size_t* used);
+int yb_tp_import(yb_engine* e, const void* blobs, size_t blob_stride);
+size_t yb_tp_blob_bytes(void);
+
+/* ---------------------------------------------------------------- kernel-level entry points
+ * Counterparts of yalm's test hooks (src/model.h:340-374: matmul_cuda, mha_cuda, ffn_cuda), with
+ * the same argument meaning: host arrays in, host arrays out, synchronous.  They allocate device
+ * memory per call and are meant for tests and tools, not for the decode loop. */
+
+/* xout (d) = W (d, n) fp16 row-major @ x (n); n % 8 == 0.  matmul_cuda<f16_t>, src/model.h:359-360 */
+int yb_matmul(float* xout, const float* x, const uint16_t* w, int n, int d);
+
+/* multi-head attention over yalm's own cache layouts (kb 16-tiled, vb [n_kv][head_dim][max_seq_len]);
+ * mha_cuda, src/model.h:348-355.  `att` is accepted for signature parity and not written. */
+int yb_mha(float* xout, float* att, const uint16_t* kb, const uint16_t* vb, const float* q, int head_dim,
+           int kv_len, int max_seq_len, int n_heads, int n_kv_heads);
+
+/* xout (dim) = W2 @ (act(W1 @ x) * (W3 @ x)) with fp16 weights; ffn_cuda<f16_t>, src/model.h:368-374
+ * (act: 0 GELU, 1 SILU). */
+int yb_ffn(float* xout, const float* x, const uint16_t* w1, const uint16_t* w2, const uint16_t* w3, int hidden_dim,
+           int dim, int act);
+
+/* ---------------------------------------------------------------- device-pointer kernel launches
+ * The individual decode kernels on caller-owned device buffers (for the kernel sweep and the
+ * parity tests).  `stream` is a cudaStream_t (NULL = legacy default stream).  Asynchronous. */
+
+/* y (rows) = W (rows, cols) @ x, or y += W @ x when accumulate != 0.  norm_w (cols) non-NULL:
+ * x is RMS-normalised first with eps (src/infer.cpp:136-146). */
+int yb_gemv_dev(float* y, const float* x, const uint16_t* w, int rows, int cols, const float* norm_w, float eps,
+                int accumulate, void* stream);
+
+/* hb (hidden) = act(W1 @ xn) * (W3 @ xn) where xn = rmsnorm(x) if norm_w != NULL; w13 holds the
+ * rows of W1 and W3 interleaved (row 2i = W1 row i, row 2i+1 = W3 row i). */
+int yb_gateup_dev(float* hb, const float* x, const uint16_t* w13, int hidden, int dim, const float* norm_w, float eps,
+                  int act, void* stream);
+
+/* Fused QKV step of one layer: [q;k;v] = Wqkv ([(n_heads + 2 n_kv_heads) head_dim, dim], the rows of
+ * Wq, Wk, Wv stacked) @ rmsnorm(x), clip, interleaved-pair RoPE at `pos`,
+ * q -> q_out (fp32), k and v -> fp16 cache slot `kv_pos` of k_cache / v_cache
+ * ([n_kv_heads][max_seq_len][head_dim]); when kv_sink > 0 also re-rotates the first kv_sink
+ * cached keys by one position (src/infer.cpp:307-325).  inv_freq_dev: head_dim/2 floats
+ * 1/theta^(2i/rotary_dim) in device memory. */
+int yb_qkv_dev(float* q_out, uint16_t* k_cache, uint16_t* v_cache, const float* x, const uint16_t* wqkv,
+               const float* norm_w, float eps, int dim, int n_heads, int n_kv_heads, int head_dim, int rotary_dim,
+               int max_seq_len, int pos, int kv_pos, int kv_sink, float qkv_clip, const float* inv_freq_dev,
+               void* stream);
+
+/* Decode attention for all heads over cache slots [0, kv_len) of k_cache / v_cache
+ * ([n_kv_heads][max_seq_len][head_dim] fp16): out (n_heads*head_dim) fp32.
+ * scratch_dev: yb_attention_scratch_bytes(...) bytes of device memory, zero-filled before its
+ * first use and left zero by every call. */
+int yb_attention_dev(float* out, const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int n_heads,
+                     int n_kv_heads, int head_dim, int max_seq_len, int kv_len, void* scratch_dev, void* stream);
+size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
+
+/* Number of streaming multiprocessors the kernels size their grids for (device 0 if none set). */
+int yb_num_sms(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* YALM_B200_H */

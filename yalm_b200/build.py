@@ -1,0 +1,84 @@
+"""In-tree build of the native libraries.
+
+  yalm_b200/libyalm_b200.so  — the decode engine (CUDA, sm_100a only) behind include/yalm_b200.h
+  yalm_b200/libyalm_synth.so — the host-side synthetic checkpoint filler used by synth.py
+
+Run `python -m yalm_b200.build` (or `__graft_entry__.build()`).  nvcc cross-compiles for sm_100a
+without a GPU.  Objects go to yalm_b200/_build/; rebuilds are incremental on source timestamps.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libyalm_b200.so")
+SYNTH_LIB = os.path.join(HERE, "libyalm_synth.so")
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
+    "-Xcompiler", "-fPIC,-O3", "-I" + os.path.join(ROOT, "include"),
+]
+CU_SOURCES = ["gemv.cu", "attention.cu", "engine.cu", "capi.cu"]
+HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "launch.h", "engine.h"]
+
+
+def _newer(target: str, deps) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def _run(cmd):
+    r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"command failed ({r.returncode}): {' '.join(cmd)}\n{r.stdout}")
+    return r.stdout
+
+
+def build_engine(verbose: bool = False, ptxas_info: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "yalm_b200.h")]
+    objs = []
+    jobs = []
+    for src in CU_SOURCES:
+        s = os.path.join(CSRC, src)
+        o = os.path.join(BUILD, src + ".o")
+        objs.append(o)
+        if _newer(o, [s] + hdrs) or ptxas_info:
+            extra = ["-Xptxas", "-v"] if ptxas_info else []
+            jobs.append([NVCC] + NVCC_FLAGS + extra + ["-c", s, "-o", o])
+    if jobs:
+        with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 4)) as ex:
+            for out in ex.map(_run, jobs):
+                if verbose or ptxas_info:
+                    sys.stdout.write(out)
+    if jobs or _newer(LIB, objs):
+        _run([NVCC] + ARCH + ["-shared", "-o", LIB] + objs)
+    return LIB
+
+
+def build_synth() -> str:
+    src = os.path.join(CSRC, "synth_fill.c")
+    if _newer(SYNTH_LIB, [src]):
+        _run(["gcc", "-O3", "-fopenmp", "-fPIC", "-shared", "-std=c11", "-o", SYNTH_LIB, src, "-lm"])
+    return SYNTH_LIB
+
+
+def build_all(verbose: bool = False) -> None:
+    build_synth()
+    build_engine(verbose=verbose)
+
+
+if __name__ == "__main__":
+    build_synth()
+    build_engine(verbose=True, ptxas_info="--ptxas" in sys.argv)
+    print(LIB)

@@ -1,0 +1,207 @@
+// Device-side building blocks shared by the decode kernels (sm_100a).
+//
+//  * mbarrier + cp.async.bulk (1-D TMA) helpers for streaming weight rows global -> shared;
+//  * programmatic dependent launch (griddepcontrol) so a kernel can start streaming its own
+//    weights while the kernel before it is still finishing;
+//  * bounded waits: every spin in this library gives up after a cycle budget, records an error
+//    code in a status word the host reads after each step, and lets the kernel return.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace yb {
+
+// Status bits written by kernels into the engine's status word (host-mapped memory).
+enum : unsigned {
+  kStatusOk = 0u,
+  kStatusMbarTimeout = 1u << 0,   // a TMA stage never landed
+  kStatusPeerTimeout = 1u << 1,   // a tensor-parallel peer never delivered its partial sums
+  kStatusBadArgs = 1u << 2,       // device-side argument check failed (e.g. position out of range)
+};
+
+// ~2 s at the B200's 1.965 GHz boost clock; a healthy wait ends within microseconds.
+constexpr long long kWaitBudgetCycles = 4000000000ll;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// Makes barrier initialisation visible to the async (TMA) proxy before the first bulk copy.
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the barrier phase with the given parity.  Returns false (and records kStatusMbarTimeout)
+// when the cycle budget runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      if (status) atomicOr(status, kStatusMbarTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- bulk copies (1-D TMA)
+// Evict-first L2 policy for data streamed exactly once per step (weights).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// global -> shared; dst, src 16-byte aligned, bytes a multiple of 16.  Completion is signalled on
+// `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, unsigned bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(dst_smem)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_nohint(void* dst_smem, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst_smem)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// Fire-and-forget prefetch of a global range into L2 (bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------- system-scope flags (peer memory)
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Waits until *p >= target (wrap-safe); false + kStatusPeerTimeout when the budget runs out.
+__device__ __forceinline__ bool wait_counter_geq(const unsigned* p, unsigned target, unsigned* status) {
+  if ((int)(ld_acquire_sys(p) - target) >= 0) return true;
+  long long t0 = clock64();
+  while ((int)(ld_acquire_sys(p) - target) < 0) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      if (status) atomicOr(status, kStatusPeerTimeout);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- named barrier among consumer warps
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------- numerics
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Reduce-scatter of N per-lane values across a warp (N a power of two, N <= 32): afterwards lane l
+// holds in v[0] the warp-wide sum of value index (l >> (5 - log2 N)).  Uses N - 1 + (5 - log2 N)
+// shuffles instead of the 5 N of N independent reductions.
+template <int N>
+__device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
+  static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N must be a power of two <= 32");
+  int cnt = N;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (cnt > 1) {
+      const int half = cnt / 2;
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) {
+        if (i < half) {
+          float send = upper ? v[i] : v[i + half];
+          float keep = upper ? v[i + half] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      cnt = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+  return v[0];
+}
+
+// 8 fp16 weights (one 16-byte vector) dotted with 8 fp32 activations, accumulated in order.
+__device__ __forceinline__ float dot8(uint4 w, const float4& xa, const float4& xb, float acc) {
+  const __half2* h = reinterpret_cast<const __half2*>(&w);
+  float2 f0 = __half22float2(h[0]);
+  float2 f1 = __half22float2(h[1]);
+  float2 f2 = __half22float2(h[2]);
+  float2 f3 = __half22float2(h[3]);
+  acc = fmaf(f0.x, xa.x, acc);
+  acc = fmaf(f0.y, xa.y, acc);
+  acc = fmaf(f1.x, xa.z, acc);
+  acc = fmaf(f1.y, xa.w, acc);
+  acc = fmaf(f2.x, xb.x, acc);
+  acc = fmaf(f2.y, xb.y, acc);
+  acc = fmaf(f3.x, xb.z, acc);
+  acc = fmaf(f3.y, xb.w, acc);
+  return acc;
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(smem_u32(p)));
+  return r;
+}
+
+// ---------------------------------------------------------------- per-step state shared by kernels
+// Written once per step by the step kernel; every later kernel of the step reads it after its
+// griddepcontrol.wait.  Positions follow yalm's ring-buffer/sink rule (src/infer.cpp:489-494).
+struct StepState {
+  int token;
+  int pos;
+  int kv_sink;
+  int kv_pos;
+  int kv_len;
+  unsigned epoch;   // forward-call counter, identical on every tensor-parallel rank
+  unsigned lepoch;  // counter of forward calls that produced logits
+  int pad;
+};
+
+}  // namespace yb

@@ -1,0 +1,721 @@
+// Decode engine: one GPU (or one tensor-parallel rank), a fixed .yalm architecture, one stream.
+//
+// Per step the engine replays one CUDA graph (separate graphs for the two InferenceModes, like
+// yalm's hydrate/output graphs, src/model.h:134-136).  The graph is
+//   step kernel (token/pos in its node parameters; writes positions + embedding row)
+//   per layer: QKV matvec (+RMSNorm, clip, RoPE, KV append, sink rotation)
+//              -> attention -> wo matvec (+residual) -> gate/up matvec (+RMSNorm, SwiGLU)
+//              -> w2 matvec (+residual)
+//   [logits mode] classifier matvec (+final RMSNorm)
+// with programmatic-dependent-launch edges between consecutive kernels.  Under tensor parallelism
+// the wo/w2 matvecs push their partial rows into every rank's exchange slots over NVLink peer
+// memory and the following matvec adds them up (no separate collective kernel).
+#include "engine.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+namespace yb {
+
+static thread_local std::string t_last_error;
+int set_error(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+const std::string& last_error() { return t_last_error; }
+
+__global__ void step_kernel(const StepArgs a) {
+  pdl_trigger();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    // src/infer.cpp:489-494
+    StepState s;
+    s.token = a.token;
+    s.pos = a.pos;
+    s.kv_sink = a.pos >= a.max_seq_len ? 2 : 0;
+    s.kv_pos = s.kv_sink + (a.pos - s.kv_sink) % (a.max_seq_len - s.kv_sink);
+    s.kv_len = a.pos >= a.max_seq_len ? a.max_seq_len : a.pos + 1;
+    s.epoch = a.epoch;
+    s.lepoch = a.lepoch;
+    s.pad = 0;
+    *a.step = s;
+  }
+  // embedding row -> fp32 residual stream (src/infer.cpp:460-481)
+  const __half* row = a.emb + (size_t)a.token * a.dim;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.dim; i += gridDim.x * blockDim.x)
+    a.x[i] = __half2float(row[i]);
+}
+
+// Kernel that waits (bounded) for every rank's slice of the gathered logits.
+__global__ void tp_gather_wait_kernel(const StepState* step, const unsigned* counters, int tp_size, int grid,
+                                      unsigned* status) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x < tp_size) wait_counter_geq(counters + threadIdx.x, step->lepoch * (unsigned)grid, status);
+}
+
+namespace {
+
+template <typename T>
+int dev_alloc(yb_engine* e, T** p, size_t bytes) {
+  void* v = nullptr;
+  cudaError_t err = cudaMalloc(&v, bytes ? bytes : 16);
+  if (err != cudaSuccess) return set_error(YB_E_CUDA, std::string("cudaMalloc(") + std::to_string(bytes) + ") failed: " + cudaGetErrorString(err));
+  e->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return 0;
+}
+
+int check_config(const yb_config* c, int tp_size) {
+  if (!c) return set_error(YB_E_INVALID, "null config");
+  if (c->weight_dtype != 1) return set_error(YB_E_UNSUPPORTED, "only fp16 weights (dtype F16) are supported");
+  if (c->n_experts != 0) return set_error(YB_E_UNSUPPORTED, "mixture-of-experts checkpoints are not supported");
+  if (c->dim <= 0 || c->hidden_dim <= 0 || c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 ||
+      c->vocab_size <= 0 || c->max_seq_len <= 2)
+    return set_error(YB_E_INVALID, "non-positive dimension in config");
+  if (c->head_dim != 64 && c->head_dim != 128) return set_error(YB_E_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (c->n_heads % c->n_kv_heads) return set_error(YB_E_INVALID, "n_heads must be a multiple of n_kv_heads");
+  const int gq = c->n_heads / c->n_kv_heads;
+  if (gq != 1 && gq != 2 && gq != 4 && gq != 8) return set_error(YB_E_UNSUPPORTED, "n_heads / n_kv_heads must be 1, 2, 4 or 8");
+  if (c->rotary_dim < 0 || c->rotary_dim > c->head_dim || (c->rotary_dim & 1))
+    return set_error(YB_E_INVALID, "rotary_dim must be even and <= head_dim");
+  if (c->dim % 8 || c->hidden_dim % 8) return set_error(YB_E_UNSUPPORTED, "dim and hidden_dim must be multiples of 8");
+  if (c->act != 0 && c->act != 1) return set_error(YB_E_INVALID, "act must be 0 (gelu) or 1 (silu)");
+  if (tp_size < 1 || c->n_kv_heads % tp_size || c->hidden_dim % (8 * tp_size) || c->vocab_size % tp_size)
+    return set_error(YB_E_INVALID, "tp_size must divide n_kv_heads, vocab_size and hidden_dim/8");
+  return 0;
+}
+
+// H2D copy of `rows` rows of `width` bytes from a host matrix with pitch spitch into a device
+// matrix with pitch dpitch.
+int copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t rows) {
+  YB_CK(cudaMemcpy2D(dst, dpitch, src, spitch, width, rows, cudaMemcpyHostToDevice));
+  return 0;
+}
+
+}  // namespace
+
+static int upload_weights(yb_engine* e, const yb_weights* w) {
+  const yb_config& c = e->cfg;
+  const int r = e->tp_rank;
+  const size_t dim = c.dim, hd = c.head_dim;
+  const size_t q_dim = (size_t)c.n_heads * hd, kv_dim = (size_t)c.n_kv_heads * hd;
+  int rc;
+  if ((rc = dev_alloc(e, &e->emb, (size_t)c.vocab_size * dim * 2))) return rc;
+  YB_CK(cudaMemcpy(e->emb, w->token_embedding_table, (size_t)c.vocab_size * dim * 2, cudaMemcpyHostToDevice));
+  if ((rc = dev_alloc(e, &e->rms_final, dim * 4))) return rc;
+  YB_CK(cudaMemcpy(e->rms_final, w->rms_final_weight, dim * 4, cudaMemcpyHostToDevice));
+  if (e->tp_size == 1 && w->wcls == w->token_embedding_table) {
+    e->wcls = e->emb;  // tied embeddings
+  } else {
+    if ((rc = dev_alloc(e, &e->wcls, (size_t)e->vocab_l * dim * 2))) return rc;
+    YB_CK(cudaMemcpy(e->wcls, w->wcls + (size_t)r * e->vocab_l * dim, (size_t)e->vocab_l * dim * 2,
+                     cudaMemcpyHostToDevice));
+  }
+  e->layers.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerBuffers& L = e->layers[l];
+    if (!w->wq[l] || !w->wk[l] || !w->wv[l] || !w->wo[l] || !w->w1[l] || !w->w2[l] || !w->w3[l] ||
+        !w->rms_att_weight[l] || !w->rms_ffn_weight[l])
+      return set_error(YB_E_INVALID, "missing tensor for layer " + std::to_string(l));
+    if ((rc = dev_alloc(e, &L.rms_att, dim * 4))) return rc;
+    if ((rc = dev_alloc(e, &L.rms_ffn, dim * 4))) return rc;
+    YB_CK(cudaMemcpy(L.rms_att, w->rms_att_weight[l], dim * 4, cudaMemcpyHostToDevice));
+    YB_CK(cudaMemcpy(L.rms_ffn, w->rms_ffn_weight[l], dim * 4, cudaMemcpyHostToDevice));
+    // [Wq rows of this rank's heads; Wk rows; Wv rows]
+    const size_t qr = e->q_rows, kr = e->kv_rows;
+    if ((rc = dev_alloc(e, &L.wqkv, (qr + 2 * kr) * dim * 2))) return rc;
+    YB_CK(cudaMemcpy(L.wqkv, w->wq[l] + (size_t)r * qr * dim, qr * dim * 2, cudaMemcpyHostToDevice));
+    YB_CK(cudaMemcpy(L.wqkv + qr * dim, w->wk[l] + (size_t)r * kr * dim, kr * dim * 2, cudaMemcpyHostToDevice));
+    YB_CK(cudaMemcpy(L.wqkv + (qr + kr) * dim, w->wv[l] + (size_t)r * kr * dim, kr * dim * 2, cudaMemcpyHostToDevice));
+    // Wo columns of this rank's heads
+    if ((rc = dev_alloc(e, &L.wo, dim * qr * 2))) return rc;
+    if ((rc = copy2d(L.wo, qr * 2, w->wo[l] + (size_t)r * qr, q_dim * 2, qr * 2, dim))) return rc;
+    // W1 / W3 rows of this rank's hidden slice, interleaved
+    const size_t h = e->hid;
+    if ((rc = dev_alloc(e, &L.w13, 2 * h * dim * 2))) return rc;
+    if ((rc = copy2d(L.w13, 2 * dim * 2, w->w1[l] + (size_t)r * h * dim, dim * 2, dim * 2, h))) return rc;
+    if ((rc = copy2d(L.w13 + dim, 2 * dim * 2, w->w3[l] + (size_t)r * h * dim, dim * 2, dim * 2, h))) return rc;
+    // W2 columns of the hidden slice
+    if ((rc = dev_alloc(e, &L.w2, dim * h * 2))) return rc;
+    if ((rc = copy2d(L.w2, h * 2, w->w2[l] + (size_t)r * h, (size_t)c.hidden_dim * 2, h * 2, dim))) return rc;
+    // KV cache, zero-initialised like yalm's (src/model.cpp:203-204)
+    const size_t kvb = (size_t)e->nkv * c.max_seq_len * hd * 2;
+    if ((rc = dev_alloc(e, &L.k_cache, kvb))) return rc;
+    if ((rc = dev_alloc(e, &L.v_cache, kvb))) return rc;
+    YB_CK(cudaMemset(L.k_cache, 0, kvb));
+    YB_CK(cudaMemset(L.v_cache, 0, kvb));
+    (void)kv_dim;
+  }
+  return 0;
+}
+
+static GemvArgs base_args(yb_engine* e) {
+  GemvArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.status = e->status_d;
+  a.step = e->step;
+  a.eps = e->cfg.norm_eps;
+  a.tp_size = e->tp_size;
+  return a;
+}
+
+int record_step(yb_engine* e, int mode, const StepArgs& sa) {
+  const yb_config& c = e->cfg;
+  cudaStream_t s = e->stream;
+  {
+    StepArgs a = sa;
+    YB_CK(launch_kernel(reinterpret_cast<const void*>(&step_kernel), dim3(4), dim3(1024), 0, s, false, &a));
+  }
+  const bool tp = e->tp_size > 1;
+  const int pf = e->tune.l2_prefetch_stages;
+  float* x_cur = e->x;  // TP: the residual stream ping-pongs between x and x2
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerBuffers& L = e->layers[l];
+    // ---- QKV
+    {
+      GemvArgs a = base_args(e);
+      a.w = L.wqkv;
+      a.ldw = c.dim;
+      a.rows = e->q_rows + 2 * e->kv_rows;
+      a.cols = c.dim;
+      a.x = x_cur;
+      a.norm_w = L.rms_att;
+      a.y = e->q;
+      a.q_rows = e->q_rows;
+      a.kv_rows = e->kv_rows;
+      a.head_dim = c.head_dim;
+      a.rotary_dim = c.rotary_dim;
+      a.max_seq_len = c.max_seq_len;
+      a.qkv_clip = c.qkv_clip;
+      a.inv_freq = e->inv_freq;
+      a.k_cache = L.k_cache;
+      a.v_cache = L.v_cache;
+      if (tp && l > 0) {
+        // add the previous layer's w2 partials (exchange point 2l-1)
+        const int pt = 2 * l - 1;
+        a.tp_slots = reinterpret_cast<const float*>(static_cast<char*>(e->tp.base) + e->tp.x_off) + (size_t)pt * e->tp_size * c.dim;
+        a.tp_counters = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) + (size_t)pt * e->tp_size;
+        a.tp_in_grid = e->plan_w2.grid;
+        float* x_next = (x_cur == e->x) ? e->x2 : e->x;
+        a.x_out = x_next;
+        x_cur = x_next;
+      }
+      YB_CK(gemv_launch(e->plan_qkv, a, s, true, pf));
+    }
+    // ---- attention
+    {
+      AttnArgs a;
+      std::memset(&a, 0, sizeof(a));
+      a.q = e->q;
+      a.k_cache = L.k_cache;
+      a.v_cache = L.v_cache;
+      a.out = e->att;
+      a.part = e->attn_part;
+      a.counters = e->attn_cnt;
+      a.step = e->step;
+      a.max_seq_len = c.max_seq_len;
+      a.status = e->status_d;
+      YB_CK(attn_launch(e->plan_attn, a, s, true));
+    }
+    // ---- wo (+ residual, or partials to peers)
+    {
+      GemvArgs a = base_args(e);
+      a.w = L.wo;
+      a.ldw = e->q_rows;
+      a.rows = c.dim;
+      a.cols = e->q_rows;
+      a.x = e->att;
+      if (tp) {
+        const int pt = 2 * l;
+        a.peer_slots = e->tp.d_peer_slots + (size_t)pt * e->tp_size;
+        a.peer_counters = e->tp.d_peer_counters + (size_t)pt * e->tp_size;
+        a.row_offset = 0;
+      } else {
+        a.y = x_cur;
+      }
+      YB_CK(gemv_launch(e->plan_wo, a, s, true, pf));
+    }
+    // ---- gate/up (+ RMSNorm, SwiGLU)
+    {
+      GemvArgs a = base_args(e);
+      a.w = L.w13;
+      a.ldw = c.dim;
+      a.rows = 2 * e->hid;
+      a.cols = c.dim;
+      a.x = x_cur;
+      a.norm_w = L.rms_ffn;
+      a.y = e->hb;
+      a.act_silu = c.act;
+      if (tp) {
+        const int pt = 2 * l;
+        a.tp_slots = reinterpret_cast<const float*>(static_cast<char*>(e->tp.base) + e->tp.x_off) + (size_t)pt * e->tp_size * c.dim;
+        a.tp_counters = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) + (size_t)pt * e->tp_size;
+        a.tp_in_grid = e->plan_wo.grid;
+        float* x_next = (x_cur == e->x) ? e->x2 : e->x;
+        a.x_out = x_next;
+        x_cur = x_next;
+      }
+      YB_CK(gemv_launch(e->plan_gu, a, s, true, pf));
+    }
+    // ---- w2 (+ residual, or partials to peers); column panels when hidden_l > 14336
+    {
+      const int panels = e->w2_panels;
+      const int pcols = e->hid / panels;
+      for (int p = 0; p < panels; ++p) {
+        GemvArgs a = base_args(e);
+        a.w = L.w2 + (size_t)p * pcols;
+        a.ldw = e->hid;
+        a.rows = c.dim;
+        a.cols = pcols;
+        a.x = e->hb + (size_t)p * pcols;
+        if (tp) {
+          const int pt = 2 * l + 1;
+          a.peer_slots = e->tp.d_peer_slots + (size_t)pt * e->tp_size;
+          a.peer_counters = e->tp.d_peer_counters + (size_t)pt * e->tp_size;
+        } else {
+          a.y = x_cur;
+        }
+        YB_CK(gemv_launch(e->plan_w2, a, s, true, pf));
+      }
+    }
+  }
+  if (mode == YB_MODE_OUTPUT_LOGITS) {
+    GemvArgs a = base_args(e);
+    a.w = e->wcls;
+    a.ldw = c.dim;
+    a.rows = e->vocab_l;
+    a.cols = c.dim;
+    a.x = x_cur;
+    a.norm_w = e->rms_final;
+    if (tp) {
+      const int pt = 2 * c.n_layers - 1;
+      a.tp_slots = reinterpret_cast<const float*>(static_cast<char*>(e->tp.base) + e->tp.x_off) + (size_t)pt * e->tp_size * c.dim;
+      a.tp_counters = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) + (size_t)pt * e->tp_size;
+      a.tp_in_grid = e->plan_w2.grid;
+      const int gp = 2 * c.n_layers;  // gather point
+      a.peer_slots = e->tp.d_peer_slots + (size_t)gp * e->tp_size;
+      a.peer_counters = e->tp.d_peer_counters + (size_t)gp * e->tp_size;
+      a.row_offset = e->tp_rank * e->vocab_l;
+    } else {
+      a.y = e->logits;
+    }
+    YB_CK(gemv_launch(e->plan_cls, a, s, true, pf));
+    if (tp) {
+      const unsigned* cnt = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) +
+                            (size_t)(2 * c.n_layers) * e->tp_size;
+      struct {
+        const StepState* step;
+        const unsigned* counters;
+        int tp_size;
+        int grid;
+        unsigned* status;
+      } wa = {e->step, cnt, e->tp_size, e->plan_cls.grid, e->status_d};
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1);
+      cfg.blockDim = dim3(32);
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      YB_CK(cudaLaunchKernelEx(&cfg, tp_gather_wait_kernel, wa.step, wa.counters, wa.tp_size, wa.grid, wa.status));
+    }
+  }
+  return 0;
+}
+
+static int build_graph(yb_engine* e, int mode) {
+  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, 0, 0, e->cfg.max_seq_len, 0, 0};
+  cudaGraph_t g = nullptr;
+  YB_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = record_step(e, mode, sa);
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return set_error(YB_E_CUDA, std::string("cudaStreamEndCapture: ") + cudaGetErrorString(ce));
+  size_t n_roots = 0;
+  YB_CK(cudaGraphGetRootNodes(g, nullptr, &n_roots));
+  if (n_roots != 1) {
+    cudaGraphDestroy(g);
+    return set_error(YB_E_CUDA, "unexpected graph shape: " + std::to_string(n_roots) + " root nodes");
+  }
+  cudaGraphNode_t root;
+  YB_CK(cudaGraphGetRootNodes(g, &root, &n_roots));
+  e->step_node[mode] = root;
+  cudaError_t ie = cudaGraphInstantiate(&e->exec[mode], g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return set_error(YB_E_CUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(ie));
+  return 0;
+}
+
+}  // namespace yb
+
+using namespace yb;
+
+static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, int device, int tp_rank, int tp_size) {
+  int rc = check_config(cfg, tp_size);
+  if (rc) return rc;
+  if (!w) return set_error(YB_E_INVALID, "null weights");
+  if (tp_rank < 0 || tp_rank >= tp_size) return set_error(YB_E_INVALID, "tp_rank out of range");
+  e->cfg = *cfg;
+  e->device = device;
+  e->tp_rank = tp_rank;
+  e->tp_size = tp_size;
+  const yb_config& c = e->cfg;
+  e->nh = c.n_heads / tp_size;
+  e->nkv = c.n_kv_heads / tp_size;
+  e->q_rows = e->nh * c.head_dim;
+  e->kv_rows = e->nkv * c.head_dim;
+  e->hid = c.hidden_dim / tp_size;
+  e->vocab_l = c.vocab_size / tp_size;
+  YB_CK(cudaSetDevice(device));
+  YB_CK(cudaDeviceGetAttribute(&e->n_sms, cudaDevAttrMultiProcessorCount, device));
+  YB_CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  YB_CK(cudaHostAlloc(reinterpret_cast<void**>(&e->status_h), 64, cudaHostAllocMapped));
+  std::memset(e->status_h, 0, 64);
+  YB_CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->status_d), e->status_h, 0));
+
+  if ((rc = upload_weights(e, w))) return rc;
+
+  // RoPE frequencies exactly as yalm computes them: 1 / powf(theta, j / rotary_dim) for even j
+  // (src/infer.cpp:205), here once on the host.
+  std::vector<float> inv(c.head_dim / 2, 0.f);
+  for (int j = 0; j < c.head_dim; j += 2)
+    inv[j / 2] = j >= c.rotary_dim ? 0.f : 1.0f / powf(c.rope_theta, (float)j / (float)c.rotary_dim);
+  if ((rc = dev_alloc(e, &e->inv_freq, inv.size() * 4))) return rc;
+  YB_CK(cudaMemcpy(e->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice));
+
+  if ((rc = dev_alloc(e, &e->x, (size_t)c.dim * 4))) return rc;
+  if ((rc = dev_alloc(e, &e->x2, (size_t)c.dim * 4))) return rc;
+  if ((rc = dev_alloc(e, &e->q, (size_t)e->q_rows * 4))) return rc;
+  if ((rc = dev_alloc(e, &e->att, (size_t)e->q_rows * 4))) return rc;
+  if ((rc = dev_alloc(e, &e->hb, (size_t)e->hid * 4))) return rc;
+  if ((rc = dev_alloc(e, &e->logits, (size_t)c.vocab_size * 4))) return rc;
+  if ((rc = dev_alloc(e, &e->step, sizeof(StepState)))) return rc;
+  YB_CK(cudaMemset(e->x, 0, (size_t)c.dim * 4));
+  YB_CK(cudaMemset(e->x2, 0, (size_t)c.dim * 4));
+  YB_CK(cudaMemset(e->step, 0, sizeof(StepState)));
+
+  // kernel plans
+  const int epi_res = tp_size > 1 ? kEpiResidTP : kEpiResid;
+  e->plan_qkv = gemv_plan(e->q_rows + 2 * e->kv_rows, c.dim, kEpiQKV, true, e->n_sms, e->tune);
+  e->plan_wo = gemv_plan(c.dim, e->q_rows, epi_res, false, e->n_sms, e->tune);
+  e->plan_gu = gemv_plan(2 * e->hid, c.dim, kEpiGateUp, true, e->n_sms, e->tune);
+  e->w2_panels = 1;
+  while (gemv_kpt_for(e->hid / e->w2_panels) < 0 || (e->hid / e->w2_panels) % 8 || e->hid % e->w2_panels) {
+    if (++e->w2_panels > 16) return set_error(YB_E_UNSUPPORTED, "hidden_dim too large");
+  }
+  if (tp_size > 1 && e->w2_panels > 1) return set_error(YB_E_UNSUPPORTED, "hidden_dim per rank too large for tensor parallelism");
+  e->plan_w2 = gemv_plan(c.dim, e->hid / e->w2_panels, epi_res, false, e->n_sms, e->tune);
+  e->plan_cls = gemv_plan(e->vocab_l, c.dim, tp_size > 1 ? kEpiStoreTP : kEpiStore, true, e->n_sms, e->tune);
+  e->plan_attn = attn_plan(e->nh, e->nkv, c.head_dim, c.max_seq_len);
+  if (!e->plan_qkv.ok || !e->plan_wo.ok || !e->plan_gu.ok || !e->plan_w2.ok || !e->plan_cls.ok || !e->plan_attn.ok)
+    return set_error(YB_E_UNSUPPORTED, "no kernel configuration for this model shape");
+  for (const GemvPlan* p : {&e->plan_qkv, &e->plan_wo, &e->plan_gu, &e->plan_w2, &e->plan_cls})
+    YB_CK(gemv_prepare(*p));
+  YB_CK(attn_prepare(e->plan_attn));
+  if ((rc = dev_alloc(e, &e->attn_part, e->plan_attn.part_floats * 4))) return rc;
+  if ((rc = dev_alloc(e, &e->attn_cnt, (size_t)e->nkv * 4))) return rc;
+  YB_CK(cudaMemset(e->attn_cnt, 0, (size_t)e->nkv * 4));
+
+  if (tp_size > 1) {
+    // exchange region: partial-sum slots, gathered logits, arrival counters
+    TpRegion& t = e->tp;
+    const size_t n_pts = 2 * (size_t)c.n_layers;
+    t.x_off = 0;
+    t.logit_off = n_pts * tp_size * c.dim * 4;
+    t.cnt_off = t.logit_off + (size_t)c.vocab_size * 4;
+    t.bytes = t.cnt_off + (n_pts + 1) * tp_size * 4;
+    t.bytes = (t.bytes + 4095) / 4096 * 4096;
+    YB_CK(cudaMalloc(&t.base, t.bytes));
+    YB_CK(cudaMemset(t.base, 0, t.bytes));
+    // graphs are recorded in yb_tp_import once the peers are mapped
+    YB_CK(cudaDeviceSynchronize());
+    return 0;
+  }
+  if ((rc = build_graph(e, 0))) return rc;
+  if ((rc = build_graph(e, 1))) return rc;
+  YB_CK(cudaDeviceSynchronize());
+  return 0;
+}
+
+extern "C" int yb_create(const yb_config* cfg, const yb_weights* w, int device, int tp_rank, int tp_size,
+                         yb_engine** out) {
+  if (!out) return set_error(YB_E_INVALID, "null output pointer");
+  *out = nullptr;
+  yb_engine* e = new yb_engine();
+  int rc = engine_init(e, cfg, w, device, tp_rank, tp_size);
+  if (rc) {
+    std::string msg = last_error();
+    yb_destroy(e);
+    return set_error(rc, msg);
+  }
+  *out = e;
+  return 0;
+}
+
+static int launch_step(yb_engine* e, int token, int pos, int mode) {
+  if (!e) return set_error(YB_E_INVALID, "null engine");
+  if (mode != 0 && mode != 1) return set_error(YB_E_INVALID, "mode must be 0 (hydrate) or 1 (logits)");
+  if (token < 0 || token >= e->cfg.vocab_size) return set_error(YB_E_INVALID, "token out of range");
+  if (pos < 0) return set_error(YB_E_INVALID, "negative position");
+  if (!e->exec[mode]) return set_error(YB_E_INVALID, "engine not ready (tensor-parallel engines need yb_tp_import)");
+  YB_CK(cudaSetDevice(e->device));
+  e->epoch += 1;
+  if (mode == YB_MODE_OUTPUT_LOGITS) e->lepoch += 1;
+  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, token, pos, e->cfg.max_seq_len, e->epoch, e->lepoch};
+  cudaKernelNodeParams kp = {};
+  void* params[] = {&sa};
+  kp.func = reinterpret_cast<void*>(&step_kernel);
+  kp.gridDim = dim3(4);
+  kp.blockDim = dim3(1024);
+  kp.sharedMemBytes = 0;
+  kp.kernelParams = params;
+  YB_CK(cudaGraphExecKernelNodeSetParams(e->exec[mode], e->step_node[mode], &kp));
+  YB_CK(cudaGraphLaunch(e->exec[mode], e->stream));
+  return 0;
+}
+
+static int check_status(yb_engine* e) {
+  const unsigned st = *reinterpret_cast<volatile unsigned*>(e->status_h);
+  if (st) {
+    char buf[160];
+    std::snprintf(buf, sizeof(buf), "device status 0x%x (1: TMA stage wait timed out, 2: peer wait timed out, 4: bad args)", st);
+    return set_error(YB_E_TIMEOUT, buf);
+  }
+  return 0;
+}
+
+extern "C" int yb_forward(yb_engine* e, int token, int pos, int mode, float* logits) {
+  int rc = launch_step(e, token, pos, mode);
+  if (rc) return rc;
+  if (mode == YB_MODE_OUTPUT_LOGITS) {
+    if (logits)
+      YB_CK(cudaMemcpyAsync(logits, yb_logits_dev(e), (size_t)e->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, e->stream));
+    YB_CK(cudaStreamSynchronize(e->stream));
+    return check_status(e);
+  }
+  return 0;
+}
+
+extern "C" int yb_forward_async(yb_engine* e, int token, int pos, int mode) { return launch_step(e, token, pos, mode); }
+
+extern "C" int yb_sync(yb_engine* e) {
+  if (!e) return set_error(YB_E_INVALID, "null engine");
+  YB_CK(cudaSetDevice(e->device));
+  YB_CK(cudaStreamSynchronize(e->stream));
+  return check_status(e);
+}
+
+extern "C" const float* yb_logits_dev(yb_engine* e) {
+  if (!e) return nullptr;
+  return e->tp_size > 1 ? reinterpret_cast<const float*>(static_cast<char*>(e->tp.base) + e->tp.logit_off) : e->logits;
+}
+
+extern "C" void* yb_stream(yb_engine* e) { return e ? static_cast<void*>(e->stream) : nullptr; }
+
+extern "C" int yb_read_kv(yb_engine* e, int layer, int kv_head, int slot0, int n, uint16_t* k_out, uint16_t* v_out) {
+  if (!e) return set_error(YB_E_INVALID, "null engine");
+  if (layer < 0 || layer >= e->cfg.n_layers || kv_head < 0 || kv_head >= e->nkv || slot0 < 0 || n < 0 ||
+      slot0 + n > e->cfg.max_seq_len)
+    return set_error(YB_E_INVALID, "read_kv range out of bounds");
+  YB_CK(cudaSetDevice(e->device));
+  YB_CK(cudaStreamSynchronize(e->stream));
+  const size_t hd = e->cfg.head_dim;
+  const size_t off = ((size_t)kv_head * e->cfg.max_seq_len + slot0) * hd;
+  if (k_out) YB_CK(cudaMemcpy(k_out, e->layers[layer].k_cache + off, (size_t)n * hd * 2, cudaMemcpyDeviceToHost));
+  if (v_out) YB_CK(cudaMemcpy(v_out, e->layers[layer].v_cache + off, (size_t)n * hd * 2, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+extern "C" unsigned yb_status(yb_engine* e) { return e ? *reinterpret_cast<volatile unsigned*>(e->status_h) : 0u; }
+
+extern "C" int yb_clear_status(yb_engine* e) {
+  if (!e) return set_error(YB_E_INVALID, "null engine");
+  *reinterpret_cast<volatile unsigned*>(e->status_h) = 0u;
+  return 0;
+}
+
+extern "C" void yb_destroy(yb_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (int m = 0; m < 2; ++m)
+    if (e->exec[m]) cudaGraphExecDestroy(e->exec[m]);
+  for (size_t i = 0; i < e->tp.peer_base.size(); ++i)
+    if ((int)i != e->tp_rank && e->tp.peer_base[i]) cudaIpcCloseMemHandle(e->tp.peer_base[i]);
+  if (e->tp.d_peer_slots) cudaFree(e->tp.d_peer_slots);
+  if (e->tp.d_peer_counters) cudaFree(e->tp.d_peer_counters);
+  if (e->tp.base) cudaFree(e->tp.base);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->status_h) cudaFreeHost(e->status_h);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+extern "C" int yb_profile_kernel(yb_engine* e, int which, int iters, float* ms_per_launch) {
+  if (!e || !ms_per_launch || iters <= 0 || which < 0 || which > 5) return set_error(YB_E_INVALID, "bad profile arguments");
+  if (e->tp_size > 1) return set_error(YB_E_INVALID, "profiling is for single-GPU engines");
+  YB_CK(cudaSetDevice(e->device));
+  const yb_config& c = e->cfg;
+  cudaEvent_t a, b;
+  YB_CK(cudaEventCreate(&a));
+  YB_CK(cudaEventCreate(&b));
+  int rc = 0;
+  auto one = [&](int i) -> int {
+    const int l = i % c.n_layers;
+    LayerBuffers& L = e->layers[l];
+    const int pf = e->tune.l2_prefetch_stages;
+    GemvArgs g = base_args(e);
+    switch (which) {
+      case 0:
+        g.w = L.wqkv; g.ldw = c.dim; g.rows = e->q_rows + 2 * e->kv_rows; g.cols = c.dim; g.x = e->x;
+        g.norm_w = L.rms_att; g.y = e->q; g.q_rows = e->q_rows; g.kv_rows = e->kv_rows; g.head_dim = c.head_dim;
+        g.rotary_dim = c.rotary_dim; g.max_seq_len = c.max_seq_len; g.qkv_clip = c.qkv_clip; g.inv_freq = e->inv_freq;
+        g.k_cache = L.k_cache; g.v_cache = L.v_cache;
+        YB_CK(gemv_launch(e->plan_qkv, g, e->stream, true, pf));
+        return 0;
+      case 1: {
+        AttnArgs t;
+        std::memset(&t, 0, sizeof(t));
+        t.q = e->q; t.k_cache = L.k_cache; t.v_cache = L.v_cache; t.out = e->att; t.part = e->attn_part;
+        t.counters = e->attn_cnt; t.step = e->step; t.max_seq_len = c.max_seq_len; t.status = e->status_d;
+        YB_CK(attn_launch(e->plan_attn, t, e->stream, true));
+        return 0;
+      }
+      case 2:
+        g.w = L.wo; g.ldw = e->q_rows; g.rows = c.dim; g.cols = e->q_rows; g.x = e->att; g.y = e->x;
+        YB_CK(gemv_launch(e->plan_wo, g, e->stream, true, pf));
+        return 0;
+      case 3:
+        g.w = L.w13; g.ldw = c.dim; g.rows = 2 * e->hid; g.cols = c.dim; g.x = e->x; g.norm_w = L.rms_ffn;
+        g.y = e->hb; g.act_silu = c.act;
+        YB_CK(gemv_launch(e->plan_gu, g, e->stream, true, pf));
+        return 0;
+      case 4: {
+        const int pcols = e->hid / e->w2_panels;
+        for (int p = 0; p < e->w2_panels; ++p) {
+          GemvArgs h = base_args(e);
+          h.w = L.w2 + (size_t)p * pcols; h.ldw = e->hid; h.rows = c.dim; h.cols = pcols;
+          h.x = e->hb + (size_t)p * pcols; h.y = e->x;
+          YB_CK(gemv_launch(e->plan_w2, h, e->stream, true, pf));
+        }
+        return 0;
+      }
+      default:
+        g.w = e->wcls; g.ldw = c.dim; g.rows = e->vocab_l; g.cols = c.dim; g.x = e->x; g.norm_w = e->rms_final;
+        g.y = e->logits;
+        YB_CK(gemv_launch(e->plan_cls, g, e->stream, true, pf));
+        return 0;
+    }
+  };
+  // one untimed pass over every layer first (first-launch costs, L2 state comparable to a step)
+  for (int i = 0; i < c.n_layers && !rc; ++i) rc = one(i);
+  if (!rc) {
+    cudaEventRecord(a, e->stream);
+    for (int i = 0; i < iters && !rc; ++i) rc = one(i);
+    cudaEventRecord(b, e->stream);
+  }
+  cudaError_t se = cudaEventSynchronize(b);
+  float ms = 0.f;
+  if (!rc && se == cudaSuccess) cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (rc) return rc;
+  if (se != cudaSuccess) return set_error(YB_E_CUDA, std::string("profile: ") + cudaGetErrorString(se));
+  *ms_per_launch = ms / (float)iters;
+  return check_status(e);
+}
+
+extern "C" int yb_last_error(char* buf, int n) {
+  const std::string& m = last_error();
+  if (buf && n > 0) {
+    std::snprintf(buf, (size_t)n, "%s", m.c_str());
+  }
+  return (int)m.size();
+}
+
+// ------------------------------------------------------------------------------ tensor parallelism
+struct TpBlob {
+  unsigned magic;
+  int rank;
+  int tp_size;
+  int pad;
+  size_t bytes;
+  cudaIpcMemHandle_t handle;
+};
+
+extern "C" size_t yb_tp_blob_bytes(void) { return sizeof(TpBlob); }
+
+extern "C" int yb_tp_export(yb_engine* e, void* blob, size_t blob_bytes, size_t* used) {
+  if (!e || !blob) return set_error(YB_E_INVALID, "null argument");
+  if (e->tp_size < 2) return set_error(YB_E_INVALID, "engine was not created for tensor parallelism");
+  if (blob_bytes < sizeof(TpBlob)) return set_error(YB_E_INVALID, "blob buffer too small");
+  YB_CK(cudaSetDevice(e->device));
+  TpBlob b;
+  std::memset(&b, 0, sizeof(b));
+  b.magic = 0x59425450u;
+  b.rank = e->tp_rank;
+  b.tp_size = e->tp_size;
+  b.bytes = e->tp.bytes;
+  YB_CK(cudaIpcGetMemHandle(&b.handle, e->tp.base));
+  std::memcpy(blob, &b, sizeof(b));
+  if (used) *used = sizeof(b);
+  return 0;
+}
+
+extern "C" int yb_tp_import(yb_engine* e, const void* blobs, size_t stride) {
+  if (!e || !blobs) return set_error(YB_E_INVALID, "null argument");
+  if (e->tp_size < 2) return set_error(YB_E_INVALID, "engine was not created for tensor parallelism");
+  if (e->tp.joined) return set_error(YB_E_INVALID, "already joined");
+  if (stride < sizeof(TpBlob)) return set_error(YB_E_INVALID, "blob stride too small");
+  YB_CK(cudaSetDevice(e->device));
+  const int P = e->tp_size;
+  const yb_config& c = e->cfg;
+  e->tp.peer_base.assign(P, nullptr);
+  for (int r = 0; r < P; ++r) {
+    TpBlob b;
+    std::memcpy(&b, static_cast<const char*>(blobs) + (size_t)r * stride, sizeof(b));
+    if (b.magic != 0x59425450u || b.rank != r || b.tp_size != P || b.bytes != e->tp.bytes)
+      return set_error(YB_E_INVALID, "inconsistent tensor-parallel blob for rank " + std::to_string(r));
+    if (r == e->tp_rank) {
+      e->tp.peer_base[r] = e->tp.base;
+    } else {
+      void* p = nullptr;
+      YB_CK(cudaIpcOpenMemHandle(&p, b.handle, cudaIpcMemLazyEnablePeerAccess));
+      e->tp.peer_base[r] = p;
+    }
+  }
+  // Destinations: at exchange point pt, rank `me` writes its partial into rank p's slot
+  // [pt][me][:] and bumps rank p's counter [pt][me].  Point 2L is the logits gather.
+  const int n_pts = 2 * c.n_layers + 1;
+  std::vector<float*> slots((size_t)n_pts * P);
+  std::vector<unsigned*> cnts((size_t)n_pts * P);
+  for (int pt = 0; pt < n_pts; ++pt) {
+    for (int p = 0; p < P; ++p) {
+      char* base = static_cast<char*>(e->tp.peer_base[p]);
+      float* dst;
+      if (pt < 2 * c.n_layers)
+        dst = reinterpret_cast<float*>(base + e->tp.x_off) + ((size_t)pt * P + e->tp_rank) * c.dim;
+      else
+        dst = reinterpret_cast<float*>(base + e->tp.logit_off);
+      slots[(size_t)pt * P + p] = dst;
+      cnts[(size_t)pt * P + p] = reinterpret_cast<unsigned*>(base + e->tp.cnt_off) + (size_t)pt * P + e->tp_rank;
+    }
+  }
+  YB_CK(cudaMalloc(&e->tp.d_peer_slots, slots.size() * sizeof(float*)));
+  YB_CK(cudaMalloc(&e->tp.d_peer_counters, cnts.size() * sizeof(unsigned*)));
+  YB_CK(cudaMemcpy(e->tp.d_peer_slots, slots.data(), slots.size() * sizeof(float*), cudaMemcpyHostToDevice));
+  YB_CK(cudaMemcpy(e->tp.d_peer_counters, cnts.data(), cnts.size() * sizeof(unsigned*), cudaMemcpyHostToDevice));
+  e->tp.joined = true;
+  int rc;
+  if ((rc = build_graph(e, 0))) return rc;
+  if ((rc = build_graph(e, 1))) return rc;
+  YB_CK(cudaDeviceSynchronize());
+  return 0;
+}

@@ -1,0 +1,107 @@
+// Host-side decode engine: weight upload/packing, device buffers, per-step CUDA graphs.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/yalm_b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "launch.h"
+
+namespace yb {
+
+int set_error(int code, const std::string& msg);
+const std::string& last_error();
+
+#define YB_CK(x)                                                                                    \
+  do {                                                                                              \
+    cudaError_t _e = (x);                                                                           \
+    if (_e != cudaSuccess)                                                                          \
+      return ::yb::set_error(YB_E_CUDA, std::string(#x) + " failed: " + cudaGetErrorString(_e));    \
+  } while (0)
+
+struct LayerBuffers {
+  __half* wqkv = nullptr;   // [q_rows + 2 kv_rows, dim]: this rank's Wq, Wk, Wv rows
+  __half* wo = nullptr;     // [dim, q_rows]: this rank's Wo columns
+  __half* w13 = nullptr;    // [2 hidden_l, dim]: W1 / W3 rows interleaved
+  __half* w2 = nullptr;     // [dim, hidden_l]: this rank's W2 columns
+  float* rms_att = nullptr;
+  float* rms_ffn = nullptr;
+  __half* k_cache = nullptr;  // [kv_heads_l][max_seq_len][head_dim]
+  __half* v_cache = nullptr;
+};
+
+// Tensor-parallel exchange region (one device allocation per rank, mapped by every peer).
+struct TpRegion {
+  void* base = nullptr;          // local allocation
+  size_t bytes = 0;
+  size_t x_off = 0;              // [2*n_layers][tp][dim] fp32 partial slots
+  size_t logit_off = 0;          // [vocab] fp32 gathered logits
+  size_t cnt_off = 0;            // [2*n_layers + 1][tp] u32 arrival counters
+  std::vector<void*> peer_base;  // per rank (own rank: base)
+  float** d_peer_slots = nullptr;      // device arrays of pointers used by kernels
+  unsigned** d_peer_counters = nullptr;
+  bool joined = false;
+};
+
+struct StepArgs {
+  StepState* step;
+  float* x;
+  const __half* emb;
+  int dim;
+  int token;
+  int pos;
+  int max_seq_len;
+  unsigned epoch;
+  unsigned lepoch;
+};
+
+}  // namespace yb
+
+struct yb_engine {
+  int device = 0;
+  int n_sms = 148;
+  cudaStream_t stream = nullptr;
+  yb_config cfg{};
+  int tp_rank = 0, tp_size = 1;
+  // local (this rank's) shapes
+  int nh = 0, nkv = 0, q_rows = 0, kv_rows = 0, hid = 0, vocab_l = 0;
+
+  std::vector<yb::LayerBuffers> layers;
+  __half* emb = nullptr;
+  __half* wcls = nullptr;
+  float* rms_final = nullptr;
+  float* inv_freq = nullptr;
+  float* x = nullptr;       // residual stream [dim] (TP: two ping-pong copies)
+  float* x2 = nullptr;
+  float* q = nullptr;       // [q_rows]
+  float* att = nullptr;     // [q_rows]
+  float* hb = nullptr;      // [hidden_l]
+  float* logits = nullptr;  // [vocab] (TP: full gathered vector)
+  float* attn_part = nullptr;
+  unsigned* attn_cnt = nullptr;
+  yb::StepState* step = nullptr;
+  unsigned* status_h = nullptr;  // host-mapped status word
+  unsigned* status_d = nullptr;
+  std::vector<void*> allocs;
+
+  yb::LaunchTuning tune;
+  yb::GemvPlan plan_qkv{}, plan_wo{}, plan_gu{}, plan_w2{}, plan_cls{};
+  int w2_panels = 1;
+  yb::AttnPlan plan_attn{};
+
+  cudaGraphExec_t exec[2] = {nullptr, nullptr};
+  cudaGraphNode_t step_node[2] = {nullptr, nullptr};
+  unsigned epoch = 0;
+  unsigned lepoch = 0;
+  yb::TpRegion tp;
+};
+
+namespace yb {
+// Records one decode step (mode 0 hydrate / 1 logits) on e->stream.  Used for graph capture.
+int record_step(yb_engine* e, int mode, const StepArgs& sa);
+}  // namespace yb

@@ -1,0 +1,412 @@
+// Weight-streaming GEMV kernels (see gemv.cuh for the design).
+#include "gemv.cuh"
+#include "launch.h"
+
+#include <cstdio>
+
+namespace yb {
+
+template <int NW, int KPT, int RT, int EPI, bool NORM>
+__global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr int NT = NW * 32;  // consumer threads
+
+  pdl_trigger();
+
+  const int T = (a.rows + RT - 1) / RT;  // stages over the whole matrix
+  const int G = gridDim.x;
+  const int s_begin = (int)((long long)T * blockIdx.x / G);
+  const int s_end = (int)((long long)T * (blockIdx.x + 1) / G);
+  const int n_st = s_end - s_begin;
+  const int row_begin = s_begin * RT;
+  const int NS = a.n_slots;
+  const unsigned SB = a.stage_bytes;
+  const int C = a.cols;
+  const unsigned row_bytes = (unsigned)C * 2u;
+
+  unsigned char* ring = smem;
+  float* red = reinterpret_cast<float*>(smem + (size_t)NS * SB);
+  float* scratch = red + a.red_floats;                    // NW floats for the norm reduction
+  uint64_t* full = reinterpret_cast<uint64_t*>(scratch + 32);
+  uint64_t* empty = full + NS;
+  __shared__ int s_abort;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NW);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == NW) {
+    // ------------------------------------------------------------------ producer
+    if (lane != 0 || n_st <= 0) return;
+    const uint64_t pol = l2_evict_first_policy();
+    const unsigned char* wbase = reinterpret_cast<const unsigned char*>(a.w);
+    const bool contiguous = (a.ldw == (long long)C);
+    // Warm L2 with the stages just beyond the ring: weights are static, so this (like the ring
+    // fill below) may run before the previous kernel of the step has finished.
+    if (contiguous && a.l2_prefetch_stages > 0) {
+      int pf_end = min(n_st, NS + a.l2_prefetch_stages);
+      for (int i = NS; i < pf_end; ++i) {
+        int row0 = row_begin + i * RT;
+        int nr = min(RT, a.rows - row0);
+        bulk_prefetch_l2(wbase + (size_t)row0 * row_bytes, (unsigned)nr * row_bytes);
+      }
+    }
+    int issued = 0;
+    for (int i = 0; i < n_st; ++i) {
+      const int slot = i % NS;
+      if (i >= NS) {
+        if (!mbar_wait(&empty[slot], ((i / NS) - 1) & 1, a.status)) {
+          s_abort = 1;
+          break;
+        }
+      }
+      const int row0 = row_begin + i * RT;
+      const int nr = min(RT, a.rows - row0);
+      mbar_arrive_expect_tx(&full[slot], (unsigned)nr * row_bytes);
+      unsigned char* dst = ring + (size_t)slot * SB;
+      if (contiguous) {
+        bulk_g2s(dst, wbase + (size_t)row0 * row_bytes, (unsigned)nr * row_bytes, &full[slot], pol);
+      } else {
+        for (int r = 0; r < nr; ++r)
+          bulk_g2s(dst + (size_t)r * row_bytes, wbase + (size_t)(row0 + r) * (size_t)a.ldw * 2u, row_bytes,
+                   &full[slot], pol);
+      }
+      issued = i + 1;
+    }
+    // Drain: never leave the CTA while a bulk copy into its shared memory may be in flight.
+    for (int i = max(0, issued - NS); i < issued; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, a.status);
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers
+  const int t = threadIdx.x;  // 0 .. NT-1
+  const int n_chunks = C >> 3;
+  float4 xr[KPT][2];
+  float4 nw[NORM ? KPT : 1][2];
+  if (NORM) {
+#pragma unroll
+    for (int k = 0; k < KPT; ++k) {
+      const int c = k * NT + t;
+      if (c < n_chunks) {
+        nw[k][0] = __ldg(reinterpret_cast<const float4*>(a.norm_w) + 2 * c);
+        nw[k][1] = __ldg(reinterpret_cast<const float4*>(a.norm_w) + 2 * c + 1);
+      }
+    }
+  }
+
+  pdl_wait();  // activations below are produced by the previous kernel of the step
+
+#pragma unroll
+  for (int k = 0; k < KPT; ++k) {
+    const int c = k * NT + t;
+    if (c < n_chunks) {
+      xr[k][0] = reinterpret_cast<const float4*>(a.x)[2 * c];
+      xr[k][1] = reinterpret_cast<const float4*>(a.x)[2 * c + 1];
+    } else {
+      xr[k][0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      xr[k][1] = xr[k][0];
+    }
+  }
+  if (a.tp_slots) {
+    // Tensor-parallel reduction of the previous row-parallel matvec: wait until every rank's CTAs
+    // have delivered their partial rows into this rank's slots, then add them in rank order (the
+    // same order on every rank, so all ranks hold bit-identical x).
+    const unsigned target = a.step->epoch * (unsigned)a.tp_in_grid;
+    if (t < a.tp_size && !wait_counter_geq(a.tp_counters + t, target, a.status)) s_abort = 1;
+    named_sync(1, NT);
+    const int w_begin = (int)((long long)n_chunks * blockIdx.x / G);
+    const int w_end = (int)((long long)n_chunks * (blockIdx.x + 1) / G);
+#pragma unroll
+    for (int k = 0; k < KPT; ++k) {
+      const int c = k * NT + t;
+      if (c < n_chunks) {
+        for (int r = 0; r < a.tp_size; ++r) {
+          const float4* sp = reinterpret_cast<const float4*>(a.tp_slots + (size_t)r * C) + 2 * c;
+          const float4 p0 = __ldcg(sp), p1 = __ldcg(sp + 1);
+          xr[k][0].x += p0.x; xr[k][0].y += p0.y; xr[k][0].z += p0.z; xr[k][0].w += p0.w;
+          xr[k][1].x += p1.x; xr[k][1].y += p1.y; xr[k][1].z += p1.z; xr[k][1].w += p1.w;
+        }
+        if (a.x_out && c >= w_begin && c < w_end) {
+          reinterpret_cast<float4*>(a.x_out)[2 * c] = xr[k][0];
+          reinterpret_cast<float4*>(a.x_out)[2 * c + 1] = xr[k][1];
+        }
+      }
+    }
+  }
+  if (NORM) {
+    // RMSNorm (yalm src/infer.cpp:136-146): scale = 1 / sqrt(mean(x^2) + eps); x * scale * w
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < KPT; ++k) {
+      ss += xr[k][0].x * xr[k][0].x + xr[k][0].y * xr[k][0].y + xr[k][0].z * xr[k][0].z + xr[k][0].w * xr[k][0].w;
+      ss += xr[k][1].x * xr[k][1].x + xr[k][1].y * xr[k][1].y + xr[k][1].z * xr[k][1].z + xr[k][1].w * xr[k][1].w;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) scratch[warp] = ss;
+    named_sync(1, NT);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) tot += scratch[w];
+    const float rms = sqrtf(tot / (float)C + a.eps);
+    const float scale = 1.0f / rms;
+#pragma unroll
+    for (int k = 0; k < KPT; ++k) {
+      const int c = k * NT + t;
+      if (c < n_chunks) {
+        xr[k][0].x = xr[k][0].x * scale * nw[k][0].x;
+        xr[k][0].y = xr[k][0].y * scale * nw[k][0].y;
+        xr[k][0].z = xr[k][0].z * scale * nw[k][0].z;
+        xr[k][0].w = xr[k][0].w * scale * nw[k][0].w;
+        xr[k][1].x = xr[k][1].x * scale * nw[k][1].x;
+        xr[k][1].y = xr[k][1].y * scale * nw[k][1].y;
+        xr[k][1].z = xr[k][1].z * scale * nw[k][1].z;
+        xr[k][1].w = xr[k][1].w * scale * nw[k][1].w;
+      }
+    }
+  }
+
+  constexpr int LOG_RT = (RT == 1) ? 0 : (RT == 2) ? 1 : (RT == 4) ? 2 : 3;
+  for (int i = 0; i < n_st; ++i) {
+    const int slot = i % NS;
+    if (!mbar_wait(&full[slot], (i / NS) & 1, a.status)) {
+      s_abort = 1;
+      break;
+    }
+    if (*(volatile int*)&s_abort) break;
+    const unsigned char* st = ring + (size_t)slot * SB;
+    const int nr = min(RT, a.rows - (row_begin + i * RT));
+    float acc[RT];
+#pragma unroll
+    for (int r = 0; r < RT; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
+      if (r < nr) {
+#pragma unroll
+        for (int k = 0; k < KPT; ++k) {
+          const int c = k * NT + t;
+          if (c < n_chunks) acc[r] = dot8(lds128(st + (size_t)r * row_bytes + (size_t)c * 16), xr[k][0], xr[k][1], acc[r]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    const float v = warp_reduce_scatter<RT>(acc, lane);
+    const int rr = lane >> (5 - LOG_RT);
+    if ((lane & ((32 >> LOG_RT) - 1)) == 0 && rr < nr) red[(i * RT + rr) * NW + warp] = v;
+  }
+  named_sync(1, NT);
+  if (s_abort) return;
+
+  // -------------------------------------------------------------------- epilogue
+  const int n_rows = min(n_st * RT, a.rows - row_begin);
+  if (EPI == kEpiStore || EPI == kEpiResid || EPI == kEpiResidTP || EPI == kEpiStoreTP) {
+    for (int lr = t; lr < n_rows; lr += NT) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) s += red[lr * NW + w];
+      const int row = row_begin + lr;
+      if (EPI == kEpiStore) {
+        a.y[row] = s;
+      } else if (EPI == kEpiResid) {
+        a.y[row] += s;
+      } else {
+        // tensor parallel: this rank's value for `row` goes to every rank's buffer
+        for (int p = 0; p < a.tp_size; ++p) a.peer_slots[p][a.row_offset + row] = s;
+      }
+    }
+    if (EPI == kEpiResidTP || EPI == kEpiStoreTP) {
+      // Publish: all partial rows of this CTA are written before the counters move.
+      __threadfence_system();
+      named_sync(1, NT);
+      if (t < a.tp_size) {
+        atomicAdd_system(a.peer_counters[t], 1u);
+      }
+    }
+  } else if (EPI == kEpiGateUp) {
+    // rows (2j, 2j+1) = (w1 row j, w3 row j); yalm src/infer.cpp:367-382
+    for (int lp = t; lp < n_rows / 2; lp += NT) {
+      float g = 0.f, u = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        g += red[(2 * lp) * NW + w];
+        u += red[(2 * lp + 1) * NW + w];
+      }
+      float act;
+      if (a.act_silu) {
+        act = g / (1.0f + expf(-g));
+      } else {
+        act = 0.5f * g * (1.0f + tanhf(0.797885f * (g + 0.044715f * g * g * g)));
+      }
+      a.y[row_begin / 2 + lp] = act * u;
+    }
+  } else if (EPI == kEpiQKV) {
+    StepState st;
+    if (a.step) {
+      st = *a.step;
+    } else {
+      st.pos = a.pos;
+      st.kv_pos = a.kv_pos;
+      st.kv_sink = a.kv_sink;
+    }
+    const int hd = a.head_dim;
+    for (int lp = t; lp < n_rows / 2; lp += NT) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        s0 += red[(2 * lp) * NW + w];
+        s1 += red[(2 * lp + 1) * NW + w];
+      }
+      // clip (src/infer.cpp:283-290)
+      s0 = s0 < -a.qkv_clip ? -a.qkv_clip : (s0 > a.qkv_clip ? a.qkv_clip : s0);
+      s1 = s1 < -a.qkv_clip ? -a.qkv_clip : (s1 > a.qkv_clip ? a.qkv_clip : s1);
+      const int gr = row_begin + 2 * lp;
+      if (gr < a.q_rows + a.kv_rows) {
+        // interleaved-pair RoPE (src/infer.cpp:202-215): angle = pos * freq_j
+        const int jh = (gr < a.q_rows ? gr : gr - a.q_rows) % hd;
+        float fcr = 1.f, fci = 0.f;
+        if (jh < a.rotary_dim) {
+          const float val = (float)st.pos * a.inv_freq[jh >> 1];
+          sincosf(val, &fci, &fcr);
+        }
+        const float r0 = s0 * fcr - s1 * fci;
+        const float r1 = s0 * fci + s1 * fcr;
+        if (gr < a.q_rows) {
+          a.y[gr] = r0;
+          a.y[gr + 1] = r1;
+        } else {
+          const int kr = gr - a.q_rows;
+          const int g = kr / hd;
+          __half* kh = a.k_cache + (size_t)g * a.max_seq_len * hd;
+          *reinterpret_cast<__half2*>(kh + (size_t)st.kv_pos * hd + jh) = __floats2half2_rn(r0, r1);
+          // attention sinks: re-rotate the kept keys by one position (src/infer.cpp:307-325)
+          if (st.kv_sink > 0 && jh < a.rotary_dim) {
+            float c1, s1v;
+            sincosf(a.inv_freq[jh >> 1], &s1v, &c1);
+            for (int r = 0; r < st.kv_sink; ++r) {
+              __half2* p = reinterpret_cast<__half2*>(kh + (size_t)r * hd + jh);
+              const float2 kv = __half22float2(*p);
+              *p = __floats2half2_rn(kv.x * c1 - kv.y * s1v, kv.x * s1v + kv.y * c1);
+            }
+          }
+        }
+      } else {
+        const int vr = gr - a.q_rows - a.kv_rows;
+        const int g = vr / hd, jh = vr % hd;
+        __half* vh = a.v_cache + (size_t)g * a.max_seq_len * hd;
+        *reinterpret_cast<__half2*>(vh + (size_t)st.kv_pos * hd + jh) = __floats2half2_rn(s0, s1);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------- host side
+namespace {
+
+template <int KPT, int RT, int EPI, bool NORM>
+const void* pick4() {
+  return reinterpret_cast<const void*>(&gemv_kernel<kGemvWarps, KPT, RT, EPI, NORM>);
+}
+// Instantiated combinations: residual epilogues never normalise their input; the tensor-parallel
+// logits epilogue always does; pair epilogues (gate/up, QKV) need at least two rows per stage.
+template <int KPT, int RT>
+const void* pick2(int epi, bool norm) {
+  constexpr int RP = RT >= 2 ? RT : 2;
+  switch (epi) {
+    case kEpiStore: return norm ? pick4<KPT, RT, kEpiStore, true>() : pick4<KPT, RT, kEpiStore, false>();
+    case kEpiResid: return norm ? nullptr : pick4<KPT, RT, kEpiResid, false>();
+    case kEpiGateUp:
+      if (RT < 2) return nullptr;
+      return norm ? pick4<KPT, RP, kEpiGateUp, true>() : pick4<KPT, RP, kEpiGateUp, false>();
+    case kEpiQKV:
+      if (RT < 2) return nullptr;
+      return norm ? pick4<KPT, RP, kEpiQKV, true>() : pick4<KPT, RP, kEpiQKV, false>();
+    case kEpiResidTP: return norm ? nullptr : pick4<KPT, RT, kEpiResidTP, false>();
+    case kEpiStoreTP: return norm ? pick4<KPT, RT, kEpiStoreTP, true>() : nullptr;
+  }
+  return nullptr;
+}
+template <int KPT>
+const void* pick1(int rt, int epi, bool norm) {
+  switch (rt) {
+    case 1: return pick2<KPT, 1>(epi, norm);
+    case 2: return pick2<KPT, 2>(epi, norm);
+    case 4: return pick2<KPT, 4>(epi, norm);
+    case 8: return pick2<KPT, 8>(epi, norm);
+  }
+  return nullptr;
+}
+const void* pick(int kpt, int rt, int epi, bool norm) {
+  switch (kpt) {
+    case 1: return pick1<1>(rt, epi, norm);
+    case 2: return pick1<2>(rt, epi, norm);
+    case 4: return pick1<4>(rt, epi, norm);
+    case 7: return pick1<7>(rt, epi, norm);
+  }
+  return nullptr;
+}
+
+}  // namespace
+
+int gemv_kpt_for(int cols) {
+  const int chunks = cols / 8;
+  const int per = (chunks + kGemvWarps * 32 - 1) / (kGemvWarps * 32);
+  if (per <= 1) return 1;
+  if (per <= 2) return 2;
+  if (per <= 4) return 4;
+  if (per <= 7) return 7;
+  return -1;
+}
+
+GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune) {
+  GemvPlan p{};
+  p.ok = false;
+  if (cols <= 0 || rows <= 0 || (cols % 8) != 0) return p;
+  p.kpt = gemv_kpt_for(cols);
+  if (p.kpt < 0) return p;
+  const int row_bytes = cols * 2;
+  int rt = 1;
+  while (rt < 8 && (rt * 2) * row_bytes <= tune.stage_bytes_target) rt *= 2;
+  const bool pairs = (epi == kEpiGateUp || epi == kEpiQKV);
+  if (pairs && rt < 2) rt = 2;
+  if (pairs && (rows % 2) != 0) return p;
+  p.rt = rt;
+  const int T = (rows + rt - 1) / rt;
+  p.grid = T < n_sms ? T : n_sms;
+  const int stages_per_cta = (T + p.grid - 1) / p.grid;
+  p.red_floats = stages_per_cta * rt * kGemvWarps;
+  p.stage_bytes = (unsigned)((rt * row_bytes + 127) / 128 * 128);
+  const int fixed = p.red_floats * 4 + 32 * 4 + 16 * 2 * 8 + 64;
+  int ns = (tune.smem_budget - fixed) / (int)p.stage_bytes;
+  if (ns > tune.max_slots) ns = tune.max_slots;
+  if (ns > stages_per_cta) ns = stages_per_cta < 2 ? 2 : stages_per_cta;
+  if (ns < 2) ns = 2;
+  p.n_slots = ns;
+  p.smem = (size_t)ns * p.stage_bytes + (size_t)p.red_floats * 4 + 32 * 4 + (size_t)ns * 2 * 8;
+  p.fn = pick(p.kpt, p.rt, epi, norm);
+  p.norm = norm;
+  p.ok = p.fn != nullptr && p.smem <= 227 * 1024;
+  return p;
+}
+
+cudaError_t gemv_prepare(const GemvPlan& p) {
+  // a cap, not a reservation: raise it to the maximum once so every plan of this instantiation fits
+  return cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages) {
+  a.stage_bytes = p.stage_bytes;
+  a.n_slots = p.n_slots;
+  a.red_floats = p.red_floats;
+  a.l2_prefetch_stages = l2_prefetch_stages;
+  return launch_kernel(p.fn, dim3(p.grid), dim3((kGemvWarps + 1) * 32), p.smem, stream, pdl, &a);
+}
+
+}  // namespace yb

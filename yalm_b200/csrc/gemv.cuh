@@ -1,0 +1,72 @@
+// Weight-streaming fp16 matrix-vector kernels for batch-1 decode.
+//
+// y = W x with W fp16 [rows, cols] row-major (row stride ldw elements), x fp32, fp32 accumulation.
+// Each CTA owns a contiguous range of rows, so the weight bytes it reads form one contiguous range
+// of HBM.  A producer warp streams that range through a ring of shared-memory stages with 1-D TMA
+// (cp.async.bulk, evict-first L2 policy); each stage holds RT whole rows.  Eight consumer warps hold
+// their slice of x in registers (thread t owns the 16-byte column chunks t, t+256, ...), so each
+// stage byte is read from shared memory exactly once.  Per stage, a warp reduce-scatter folds the
+// RT partial sums; the cross-warp sums and the fused epilogue run once at the end of the CTA.
+//
+// Kernel boundaries are hidden with programmatic dependent launch: a kernel triggers its
+// dependents on entry, its producer fills the ring (and optionally prefetches further into L2)
+// before griddepcontrol.wait, and only the consumers — which read activations written by the
+// previous kernel — wait.
+#pragma once
+
+#include "common.cuh"
+
+namespace yb {
+
+enum GemvEpilogue : int {
+  kEpiStore = 0,   // y[r] = sum                                   (classifier, plain matvec)
+  kEpiResid = 1,   // y[r] += sum                                  (wo, w2: residual into x)
+  kEpiGateUp = 2,  // rows interleaved gate/up: y[r/2] = act(gate) * up   (fused w1/w3 + SwiGLU)
+  kEpiQKV = 3,     // [q; k; v] rows: clip, RoPE, q -> fp32, k/v -> fp16 KV cache (+ sink rotation)
+  kEpiResidTP = 4, // partial sums pushed to every tensor-parallel peer's exchange slot
+  kEpiStoreTP = 5, // row sums stored at row_offset + r in every tensor-parallel peer's buffer
+};
+
+constexpr int kGemvWarps = 8;  // consumer warps; one more warp is the TMA producer
+
+struct GemvArgs {
+  const __half* w;
+  long long ldw;        // row stride of W in elements
+  int rows;
+  int cols;             // multiple of 8
+  const float* x;       // [cols]
+  const float* norm_w;  // non-null: x is RMS-normalised with this weight first (cols == dim)
+  float eps;
+  float* y;
+  unsigned* status;
+  const StepState* step;
+  // shared-memory plan (host computed)
+  unsigned stage_bytes;  // slot stride (>= RT * cols * 2, multiple of 128)
+  int n_slots;
+  int red_floats;        // rows-per-CTA upper bound * kGemvWarps
+  int l2_prefetch_stages;
+  // kEpiGateUp
+  int act_silu;
+  // kEpiQKV
+  int q_rows, kv_rows, head_dim, rotary_dim, max_seq_len;
+  float qkv_clip;
+  const float* inv_freq;  // [head_dim / 2]
+  int pos, kv_pos, kv_sink;  // used when step == nullptr (standalone launches)
+  __half* k_cache;        // [kv_heads][max_seq_len][head_dim] for this layer
+  __half* v_cache;
+  // kEpiResidTP / kEpiStoreTP: per rank, the destination base in that rank's memory and the
+  // arrival counter (for this rank) that each CTA bumps once its rows are written
+  float* const* peer_slots;
+  unsigned* const* peer_counters;
+  int tp_size;
+  int row_offset;
+  // tensor-parallel input: x_in = x + sum over ranks r (in rank order) of tp_slots[r * cols ..],
+  // after each rank's counter reached epoch * tp_in_grid.  x_out (if non-null) receives x_in,
+  // each CTA writing its share of the chunks.
+  const float* tp_slots;
+  const unsigned* tp_counters;
+  int tp_in_grid;
+  float* x_out;
+};
+
+}  // namespace yb

@@ -1,0 +1,57 @@
+// Host-side launch helpers and kernel plans shared by the engine and the C-ABI test hooks.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+
+#include "common.cuh"
+
+namespace yb {
+
+struct GemvArgs;
+struct AttnArgs;
+
+// Tunables for the streaming kernels (host values; see the engine for defaults).
+struct LaunchTuning {
+  int stage_bytes_target = 16384;  // bytes of whole rows per TMA stage
+  int smem_budget = 110 * 1024;    // per-CTA dynamic shared memory; two CTAs fit on one SM
+  int max_slots = 8;               // ring depth cap
+  int l2_prefetch_stages = 4;      // stages beyond the ring warmed into L2 before griddepcontrol.wait
+  int attn_positions_per_cta = 128;
+};
+
+struct GemvPlan {
+  bool ok;
+  const void* fn;
+  int kpt, rt, grid, n_slots, red_floats;
+  unsigned stage_bytes;
+  size_t smem;
+  bool norm;  // the kernel RMS-normalises x (GemvArgs::norm_w must then be set)
+};
+
+int gemv_kpt_for(int cols);
+GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune);
+cudaError_t gemv_prepare(const GemvPlan& p);  // once per plan, outside stream capture
+cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages);
+
+// cudaLaunchKernelEx with the programmatic-stream-serialization attribute when `pdl` is set, so the
+// kernel may begin while the previous kernel in the stream is still running (it must call
+// griddepcontrol.wait before reading that kernel's results).
+template <typename Args>
+inline cudaError_t launch_kernel(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                                 Args* args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  void* params[] = {args};
+  return cudaLaunchKernelExC(&cfg, fn, params);
+}
+
+}  // namespace yb

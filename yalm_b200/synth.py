@@ -1,0 +1,197 @@
+"""Seeded synthetic .yalm checkpoints.
+
+A .yalm file is a safetensors container: an 8-byte little-endian header length, a JSON header whose
+``__metadata__`` holds string-valued model config keys, and tensor data (yalm convert.py:22-81 for
+the keys, convert.py:164-204 and :245 for tensor names and dtypes, src/codec.cpp:97-156 for the
+reader).  This module writes files with that exact layout for the architectures in the benchmark
+configs: fp16 matrices ~ N(0, std), fp32 norm weights (1.0), an untied classifier and a synthetic
+tokenizer vocabulary.  Weight contents depend only on (seed, tensor name), so the same call always
+produces the same bytes.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import zlib
+from dataclasses import dataclass, asdict
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@dataclass(frozen=True)
+class ModelShape:
+    dim: int
+    hidden_dim: int
+    head_dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    vocab_size: int
+    max_seq_len: int
+    rope_theta: float = 1000000.0
+    norm_eps: float = 1e-05
+    act_type: str = "silu"
+    arch: str = "MistralForCausalLM"
+
+    @property
+    def q_dim(self) -> int:
+        return self.n_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+
+# The architectures of the benchmark configs.  `max_seq_len` is the metadata value; yalm caps it at
+# 4096 unless a context is given (src/model.cpp:30-34), so the 70B config is opened with context 8192.
+SHAPES = {
+    "tiny": ModelShape(dim=512, hidden_dim=1408, head_dim=64, n_layers=4, n_heads=8, n_kv_heads=2,
+                       vocab_size=4096, max_seq_len=1024),
+    "mistral-7b": ModelShape(dim=4096, hidden_dim=14336, head_dim=128, n_layers=32, n_heads=32, n_kv_heads=8,
+                             vocab_size=32000, max_seq_len=32768),
+    "llama-70b": ModelShape(dim=8192, hidden_dim=28672, head_dim=128, n_layers=80, n_heads=64, n_kv_heads=8,
+                            vocab_size=32000, max_seq_len=8192, arch="LlamaForCausalLM"),
+}
+
+
+def shape_with(base: str, **overrides) -> ModelShape:
+    d = asdict(SHAPES[base])
+    d.update(overrides)
+    return ModelShape(**d)
+
+
+def metadata(shape: ModelShape) -> dict:
+    """String-valued metadata exactly as convert.py's Metadata.to_dict (convert.py:58-81)."""
+    return {
+        "arch": shape.arch,
+        "dtype": "fp16",
+        "dim": str(shape.dim),
+        "hidden_dim": str(shape.hidden_dim),
+        "head_dim": str(shape.head_dim),
+        "n_layers": str(shape.n_layers),
+        "n_heads": str(shape.n_heads),
+        "n_kv_heads": str(shape.n_kv_heads),
+        "vocab_size": str(shape.vocab_size),
+        "max_seq_len": str(shape.max_seq_len),
+        "bos_token_id": "1",
+        "eos_token_id": "2",
+        "rope_theta": str(float(shape.rope_theta)),
+        "rotary_dim": str(shape.head_dim),
+        "norm_eps": str(shape.norm_eps),
+        "norm_type": "rmsnorm",
+        "act_type": shape.act_type,
+    }
+
+
+def tensor_specs(shape: ModelShape):
+    """(name, dtype, shape) in file order, names as convert.py writes them (convert.py:164-204)."""
+    s = shape
+    out = [("model.embed.weight", "F16", (s.vocab_size, s.dim))]
+    for l in range(s.n_layers):
+        p = f"model.layers.{l}."
+        out += [
+            (p + "attn.norm.weight", "F32", (s.dim,)),
+            (p + "attn.wq.weight", "F16", (s.q_dim, s.dim)),
+            (p + "attn.wk.weight", "F16", (s.kv_dim, s.dim)),
+            (p + "attn.wv.weight", "F16", (s.kv_dim, s.dim)),
+            (p + "attn.wo.weight", "F16", (s.dim, s.q_dim)),
+            (p + "mlp.norm.weight", "F32", (s.dim,)),
+            (p + "mlp.w1.weight", "F16", (s.hidden_dim, s.dim)),
+            (p + "mlp.w2.weight", "F16", (s.dim, s.hidden_dim)),
+            (p + "mlp.w3.weight", "F16", (s.hidden_dim, s.dim)),
+        ]
+    out += [("model.norm.weight", "F32", (s.dim,)), ("model.output.weight", "F16", (s.vocab_size, s.dim))]
+    return out
+
+
+def vocab_bytes(vocab_size: int) -> bytes:
+    """NUL-joined token strings (convert.py:245): specials, 256 byte-fallback pieces, then '~<id>'."""
+    toks = ["<unk>", "<s>", "</s>"] + [f"<0x{b:02X}>" for b in range(256)]
+    toks += [f"~{i}" for i in range(len(toks), vocab_size)]
+    toks = toks[:vocab_size]
+    return b"".join(t.encode() + b"\0" for t in toks)
+
+
+_DTYPE_SIZE = {"F16": 2, "F32": 4, "U8": 1}
+_lib = None
+
+
+def _synth_lib():
+    global _lib
+    if _lib is None:
+        path = os.path.join(_HERE, "libyalm_synth.so")
+        if not os.path.exists(path):
+            from . import build as _build
+            _build.build_synth()
+        _lib = ctypes.CDLL(path)
+        _lib.synth_fill_normal_f16.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint64,
+                                               ctypes.c_uint64, ctypes.c_float]
+        _lib.synth_fill_const_f32.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_float]
+    return _lib
+
+
+def write_yalm(path: str, shape: ModelShape, seed: int = 0, std: float = 0.02) -> str:
+    """Writes a synthetic .yalm checkpoint to `path` and returns it.  Rewrites only when the header
+    of an existing file differs (the data is a pure function of the header and seed)."""
+    specs = tensor_specs(shape)
+    tok = vocab_bytes(shape.vocab_size)
+    header = {"__metadata__": dict(metadata(shape), synth_seed=str(seed), synth_std=str(std))}
+    off = 0
+    for name, dt, shp in specs:
+        n = int(np.prod(shp)) * _DTYPE_SIZE[dt]
+        header[name] = {"dtype": dt, "shape": list(shp), "data_offsets": [off, off + n]}
+        off += n
+    header["tokenizer.tokens"] = {"dtype": "U8", "shape": [len(tok)], "data_offsets": [off, off + len(tok)]}
+    off += len(tok)
+    hjson = json.dumps(header, separators=(",", ":")).encode()
+    # pad so tensor data starts on a 256-byte boundary (spaces are valid JSON whitespace)
+    pad = (-(8 + len(hjson))) % 256
+    hjson += b" " * pad
+    data_start = 8 + len(hjson)
+    total = data_start + off
+    if os.path.exists(path) and os.path.getsize(path) == total:
+        with open(path, "rb") as f:
+            n = int.from_bytes(f.read(8), "little")
+            if f.read(n) == hjson:
+                return path
+    lib = _synth_lib()
+    tmp = path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(len(hjson).to_bytes(8, "little"))
+        f.write(hjson)
+        f.truncate(total)
+    mm = np.memmap(tmp, dtype=np.uint8, mode="r+")
+    base = mm.ctypes.data + data_start
+    for name, dt, shp in specs:
+        o0, o1 = header[name]["data_offsets"]
+        n = int(np.prod(shp))
+        if dt == "F32":
+            lib.synth_fill_const_f32(base + o0, n, 1.0)
+        else:
+            lib.synth_fill_normal_f16(base + o0, n, seed, zlib.crc32(name.encode()), std)
+    o0, _ = header["tokenizer.tokens"]["data_offsets"]
+    mm[data_start + o0: data_start + o0 + len(tok)] = np.frombuffer(tok, dtype=np.uint8)
+    mm.flush()
+    del mm
+    os.replace(tmp, path)
+    return path
+
+
+def scratch_dir(nbytes: int) -> str:
+    """A directory with room for nbytes: /dev/shm when it has space, else the system temp dir."""
+    import shutil
+    import tempfile
+    for d in ("/dev/shm", tempfile.gettempdir()):
+        try:
+            if shutil.disk_usage(d).free > nbytes * 1.1 + (1 << 30):
+                return d
+        except OSError:
+            pass
+    return tempfile.gettempdir()
+
+
+def file_bytes(shape: ModelShape) -> int:
+    return sum(int(np.prod(s)) * _DTYPE_SIZE[d] for _, d, s in tensor_specs(shape)) + len(vocab_bytes(shape.vocab_size))
