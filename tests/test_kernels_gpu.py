@@ -12,9 +12,24 @@ from yalm_b200 import _lib
 pytestmark = pytest.mark.gpu
 
 
+_ALIVE = []
+
+
 def _t(a):
+    """Device copy of a numpy array, kept alive until the test module ends (a temporary freed while
+    its kernel is still queued would be handed to the next allocation by torch's caching allocator)."""
     import torch
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _ALIVE.append(t)
+    return t
+
+
+@pytest.fixture(autouse=True)
+def _release_buffers():
+    yield
+    import torch
+    torch.cuda.synchronize()
+    _ALIVE.clear()
 
 
 def _ptr(t):
@@ -92,9 +107,20 @@ def test_gateup_swiglu(gpu, hidden, dim, act):
 
 
 def _inv_freq(head_dim, rotary_dim, theta):
-    return np.array([0.0 if j >= rotary_dim else 1.0 / np.power(np.float32(theta), np.float32(j) / np.float32(rotary_dim),
-                                                                  dtype=np.float32)
-                     for j in range(0, head_dim, 2)], np.float32)
+    """1 / powf(theta, j / rotary_dim) with the C library's powf, as yalm and the oracle compute it
+    (src/infer.cpp:205); numpy's float32 power can differ by an ulp, which at position 3000 moves
+    the RoPE angle by ~1e-4 rad."""
+    libm = ctypes.CDLL("libm.so.6")
+    libm.powf.restype = ctypes.c_float
+    libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    out = []
+    for j in range(0, head_dim, 2):
+        if j >= rotary_dim:
+            out.append(0.0)
+        else:
+            e = np.float32(j) / np.float32(rotary_dim)
+            out.append(np.float32(1.0) / np.float32(libm.powf(np.float32(theta), e)))
+    return np.array(out, np.float32)
 
 
 @pytest.mark.parametrize("nh,nkv,hd,dim,pos,msl", [(8, 2, 64, 512, 5, 64), (32, 8, 128, 4096, 3000, 4096),

@@ -42,9 +42,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
 
   const int kv_len = a.step ? a.step->kv_len : a.kv_len;
   const int s_max = gridDim.x;
+  // slices of at least one staged sub-chunk: short contexts need no merge at all
   int chunk = (kv_len + s_max - 1) / s_max;
   chunk = ((chunk + 15) / 16) * 16;
-  if (chunk < 16) chunk = 16;
+  if (chunk < kAttnSub) chunk = kAttnSub;
   const int n_act = (kv_len + chunk - 1) / chunk;
   const int t0 = sidx * chunk;
   if (t0 >= kv_len) return;  // inactive slice: not counted by the merge
@@ -283,13 +284,11 @@ AttnPlan attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len) {
   p.smem = kv + sc + 2 * 8;
   if (red > kv) return p;
   p.part_floats = (size_t)n_heads * p.s_max * (head_dim + 2);
-  p.ok = p.smem <= 227 * 1024;
+  p.ok = p.smem <= 226 * 1024;
   return p;
 }
 
-cudaError_t attn_prepare(const AttnPlan& p) {
-  return cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-}
+cudaError_t attn_prepare(const AttnPlan& p) { return raise_smem_cap(p.fn); }
 
 cudaError_t attn_launch(const AttnPlan& p, AttnArgs a, cudaStream_t stream, bool pdl) {
   return launch_kernel(p.fn, p.grid, dim3(kAttnThreads), p.smem, stream, pdl, &a);

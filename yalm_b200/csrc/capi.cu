@@ -3,6 +3,9 @@
 #include "engine.h"
 
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <vector>
 
 using namespace yb;
@@ -36,14 +39,51 @@ GemvArgs plain_args() {
   return a;
 }
 
+// Plans for standalone launches, cached per (device, shape, epilogue) so that repeated calls cost
+// one map lookup on the host.
+std::mutex g_plan_mu;
+std::map<std::tuple<int, int, int, int, bool>, GemvPlan> g_gemv_plans;
+std::map<std::tuple<int, int, int, int, int>, AttnPlan> g_attn_plans;
+
+int cached_gemv_plan(int rows, int cols, int epi, bool norm, GemvPlan* out) {
+  int dev = 0;
+  YB_CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_plan_mu);
+  auto key = std::make_tuple(dev, rows, cols, epi, norm);
+  auto it = g_gemv_plans.find(key);
+  if (it == g_gemv_plans.end()) {
+    GemvPlan p = gemv_plan(rows, cols, epi, norm, current_sms(), LaunchTuning::from_env());
+    if (!p.ok)
+      return set_error(YB_E_UNSUPPORTED,
+                       "no matvec configuration for rows=" + std::to_string(rows) + " cols=" + std::to_string(cols));
+    YB_CK(gemv_prepare(p));
+    it = g_gemv_plans.emplace(key, p).first;
+  }
+  *out = it->second;
+  return 0;
+}
+
 int launch_gemv_common(GemvArgs a, int epi, cudaStream_t s) {
-  LaunchTuning tune;
-  GemvPlan p = gemv_plan(a.rows, a.cols, epi, a.norm_w != nullptr, current_sms(), tune);
-  if (!p.ok)
-    return set_error(YB_E_UNSUPPORTED,
-                     "no matvec configuration for rows=" + std::to_string(a.rows) + " cols=" + std::to_string(a.cols));
-  YB_CK(gemv_prepare(p));
-  YB_CK(gemv_launch(p, a, s, false, tune.l2_prefetch_stages));
+  GemvPlan p;
+  int rc = cached_gemv_plan(a.rows, a.cols, epi, a.norm_w != nullptr, &p);
+  if (rc) return rc;
+  YB_CK(gemv_launch(p, a, s, false, LaunchTuning::from_env().l2_prefetch_stages));
+  return 0;
+}
+
+int cached_attn_plan(int nh, int nkv, int hd, int msl, AttnPlan* out) {
+  int dev = 0;
+  YB_CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_plan_mu);
+  auto key = std::make_tuple(dev, nh, nkv, hd, msl);
+  auto it = g_attn_plans.find(key);
+  if (it == g_attn_plans.end()) {
+    AttnPlan p = attn_plan(nh, nkv, hd, msl);
+    if (!p.ok) return set_error(YB_E_UNSUPPORTED, "no attention configuration for this shape");
+    YB_CK(attn_prepare(p));
+    it = g_attn_plans.emplace(key, p).first;
+  }
+  *out = it->second;
   return 0;
 }
 
@@ -125,8 +165,9 @@ extern "C" int yb_attention_dev(float* out, const float* q, const uint16_t* k_ca
                                 void* scratch_dev, void* stream) {
   if (!out || !q || !k_cache || !v_cache || !scratch_dev || kv_len <= 0 || kv_len > max_seq_len)
     return set_error(YB_E_INVALID, "bad attention arguments");
-  AttnPlan p = attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len);
-  if (!p.ok) return set_error(YB_E_UNSUPPORTED, "no attention configuration for this shape");
+  AttnPlan p;
+  int rc = cached_attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len, &p);
+  if (rc) return rc;
   AttnArgs a;
   std::memset(&a, 0, sizeof(a));
   a.q = q;
@@ -138,7 +179,6 @@ extern "C" int yb_attention_dev(float* out, const float* q, const uint16_t* k_ca
   a.step = nullptr;
   a.kv_len = kv_len;
   a.max_seq_len = max_seq_len;
-  YB_CK(attn_prepare(p));
   YB_CK(attn_launch(p, a, static_cast<cudaStream_t>(stream), false));
   return 0;
 }

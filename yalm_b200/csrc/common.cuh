@@ -164,22 +164,23 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
   return v[0];
 }
 
-// 8 fp16 weights (one 16-byte vector) dotted with 8 fp32 activations, accumulated in order.
-__device__ __forceinline__ float dot8(uint4 w, const float4& xa, const float4& xb, float acc) {
+// 8 fp16 weights (one 16-byte vector) dotted with 8 fp32 activations: two independent 4-long FMA
+// chains (even / odd elements), so the dependency chain is half as long.
+__device__ __forceinline__ float dot8(uint4 w, const float4& xa, const float4& xb) {
   const __half2* h = reinterpret_cast<const __half2*>(&w);
-  float2 f0 = __half22float2(h[0]);
-  float2 f1 = __half22float2(h[1]);
-  float2 f2 = __half22float2(h[2]);
-  float2 f3 = __half22float2(h[3]);
-  acc = fmaf(f0.x, xa.x, acc);
-  acc = fmaf(f0.y, xa.y, acc);
-  acc = fmaf(f1.x, xa.z, acc);
-  acc = fmaf(f1.y, xa.w, acc);
-  acc = fmaf(f2.x, xb.x, acc);
-  acc = fmaf(f2.y, xb.y, acc);
-  acc = fmaf(f3.x, xb.z, acc);
-  acc = fmaf(f3.y, xb.w, acc);
-  return acc;
+  const float2 f0 = __half22float2(h[0]);
+  const float2 f1 = __half22float2(h[1]);
+  const float2 f2 = __half22float2(h[2]);
+  const float2 f3 = __half22float2(h[3]);
+  float e = f0.x * xa.x;
+  float o = f0.y * xa.y;
+  e = fmaf(f1.x, xa.z, e);
+  o = fmaf(f1.y, xa.w, o);
+  e = fmaf(f2.x, xb.x, e);
+  o = fmaf(f2.y, xb.y, o);
+  e = fmaf(f3.x, xb.z, e);
+  o = fmaf(f3.y, xb.w, o);
+  return e + o;
 }
 
 __device__ __forceinline__ uint4 lds128(const void* p) {

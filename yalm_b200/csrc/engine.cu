@@ -347,8 +347,9 @@ static int build_graph(yb_engine* e, int mode) {
   cudaGraphNode_t root;
   YB_CK(cudaGraphGetRootNodes(g, &root, &n_roots));
   e->step_node[mode] = root;
+  // the graph stays alive: the step node handle used for per-call parameter updates belongs to it
+  e->graph[mode] = g;
   cudaError_t ie = cudaGraphInstantiate(&e->exec[mode], g, 0);
-  cudaGraphDestroy(g);
   if (ie != cudaSuccess) return set_error(YB_E_CUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(ie));
   return 0;
 }
@@ -363,6 +364,7 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
   if (!w) return set_error(YB_E_INVALID, "null weights");
   if (tp_rank < 0 || tp_rank >= tp_size) return set_error(YB_E_INVALID, "tp_rank out of range");
   e->cfg = *cfg;
+  e->tune = LaunchTuning::from_env();
   e->device = device;
   e->tp_rank = tp_rank;
   e->tp_size = tp_size;
@@ -545,8 +547,10 @@ extern "C" void yb_destroy(yb_engine* e) {
   if (!e) return;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
-  for (int m = 0; m < 2; ++m)
+  for (int m = 0; m < 2; ++m) {
     if (e->exec[m]) cudaGraphExecDestroy(e->exec[m]);
+    if (e->graph[m]) cudaGraphDestroy(e->graph[m]);
+  }
   for (size_t i = 0; i < e->tp.peer_base.size(); ++i)
     if ((int)i != e->tp_rank && e->tp.peer_base[i]) cudaIpcCloseMemHandle(e->tp.peer_base[i]);
   if (e->tp.d_peer_slots) cudaFree(e->tp.d_peer_slots);

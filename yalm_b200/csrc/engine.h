@@ -94,6 +94,7 @@ struct yb_engine {
   int w2_panels = 1;
   yb::AttnPlan plan_attn{};
 
+  cudaGraph_t graph[2] = {nullptr, nullptr};
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
   cudaGraphNode_t step_node[2] = {nullptr, nullptr};
   unsigned epoch = 0;

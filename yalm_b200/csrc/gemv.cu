@@ -3,6 +3,8 @@
 #include "launch.h"
 
 #include <cstdio>
+#include <cstdlib>
+#include <string>
 
 namespace yb {
 
@@ -183,18 +185,23 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
     if (*(volatile int*)&s_abort) break;
     const unsigned char* st = ring + (size_t)slot * SB;
     const int nr = min(RT, a.rows - (row_begin + i * RT));
+    // all shared-memory loads of the stage first, then independent per-chunk dot products
     float acc[RT];
 #pragma unroll
-    for (int r = 0; r < RT; ++r) acc[r] = 0.f;
-#pragma unroll
     for (int r = 0; r < RT; ++r) {
-      if (r < nr) {
+      uint4 wv[KPT];
 #pragma unroll
-        for (int k = 0; k < KPT; ++k) {
-          const int c = k * NT + t;
-          if (c < n_chunks) acc[r] = dot8(lds128(st + (size_t)r * row_bytes + (size_t)c * 16), xr[k][0], xr[k][1], acc[r]);
-        }
+      for (int k = 0; k < KPT; ++k) {
+        const int c = k * NT + t;
+        wv[k] = (r < nr && c < n_chunks) ? lds128(st + (size_t)r * row_bytes + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
       }
+      float part[KPT];
+#pragma unroll
+      for (int k = 0; k < KPT; ++k) part[k] = dot8(wv[k], xr[k][0], xr[k][1]);
+      float s = part[0];
+#pragma unroll
+      for (int k = 1; k < KPT; ++k) s += part[k];
+      acc[r] = s;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
@@ -355,6 +362,34 @@ const void* pick(int kpt, int rt, int epi, bool norm) {
 
 }  // namespace
 
+LaunchTuning LaunchTuning::from_env() {
+  static const LaunchTuning cached = [] {
+    LaunchTuning t;
+    const char* env = std::getenv("YB_TUNE");
+    if (!env) return t;
+    std::string s(env);
+    size_t i = 0;
+    while (i < s.size()) {
+      size_t j = s.find(',', i);
+      if (j == std::string::npos) j = s.size();
+      std::string kv = s.substr(i, j - i);
+      size_t eq = kv.find('=');
+      if (eq != std::string::npos) {
+        const std::string k = kv.substr(0, eq);
+        const int v = std::atoi(kv.c_str() + eq + 1);
+        if (k == "stage" && v >= 1024) t.stage_bytes_target = v;
+        else if (k == "budget" && v >= 16384) t.smem_budget = v;
+        else if (k == "slots" && v >= 2) t.max_slots = v;
+        else if (k == "l2pf" && v >= 0) t.l2_prefetch_stages = v;
+        else if (k == "ctas" && v >= 1 && v <= 8) t.ctas_per_sm = v;
+      }
+      i = j + 1;
+    }
+    return t;
+  }();
+  return cached;
+}
+
 int gemv_kpt_for(int cols) {
   const int chunks = cols / 8;
   const int per = (chunks + kGemvWarps * 32 - 1) / (kGemvWarps * 32);
@@ -379,27 +414,26 @@ GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const Laun
   if (pairs && (rows % 2) != 0) return p;
   p.rt = rt;
   const int T = (rows + rt - 1) / rt;
-  p.grid = T < n_sms ? T : n_sms;
+  const int max_grid = n_sms * tune.ctas_per_sm;
+  p.grid = T < max_grid ? T : max_grid;
   const int stages_per_cta = (T + p.grid - 1) / p.grid;
   p.red_floats = stages_per_cta * rt * kGemvWarps;
   p.stage_bytes = (unsigned)((rt * row_bytes + 127) / 128 * 128);
   const int fixed = p.red_floats * 4 + 32 * 4 + 16 * 2 * 8 + 64;
   int ns = (tune.smem_budget - fixed) / (int)p.stage_bytes;
   if (ns > tune.max_slots) ns = tune.max_slots;
+  if (ns > 16) ns = 16;
   if (ns > stages_per_cta) ns = stages_per_cta < 2 ? 2 : stages_per_cta;
   if (ns < 2) ns = 2;
   p.n_slots = ns;
   p.smem = (size_t)ns * p.stage_bytes + (size_t)p.red_floats * 4 + 32 * 4 + (size_t)ns * 2 * 8;
   p.fn = pick(p.kpt, p.rt, epi, norm);
   p.norm = norm;
-  p.ok = p.fn != nullptr && p.smem <= 227 * 1024;
+  p.ok = p.fn != nullptr && p.smem <= 226 * 1024;
   return p;
 }
 
-cudaError_t gemv_prepare(const GemvPlan& p) {
-  // a cap, not a reservation: raise it to the maximum once so every plan of this instantiation fits
-  return cudaFuncSetAttribute(p.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-}
+cudaError_t gemv_prepare(const GemvPlan& p) { return raise_smem_cap(p.fn); }
 
 cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages) {
   a.stage_bytes = p.stage_bytes;

@@ -14,10 +14,14 @@ struct AttnArgs;
 // Tunables for the streaming kernels (host values; see the engine for defaults).
 struct LaunchTuning {
   int stage_bytes_target = 16384;  // bytes of whole rows per TMA stage
-  int smem_budget = 110 * 1024;    // per-CTA dynamic shared memory; two CTAs fit on one SM
+  int smem_budget = 100000;        // per-CTA dynamic shared memory; two CTAs fit on one SM
   int max_slots = 8;               // ring depth cap
   int l2_prefetch_stages = 4;      // stages beyond the ring warmed into L2 before griddepcontrol.wait
-  int attn_positions_per_cta = 128;
+  int ctas_per_sm = 2;              // GEMV grid = min(stages, SMs * ctas_per_sm)
+
+  // Defaults, overridable with YB_TUNE="stage=16384,budget=112640,slots=8,l2pf=4,ctas=1" (read once
+  // per process) for tuning sweeps.
+  static LaunchTuning from_env();
 };
 
 struct GemvPlan {
@@ -33,6 +37,20 @@ int gemv_kpt_for(int cols);
 GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune);
 cudaError_t gemv_prepare(const GemvPlan& p);  // once per plan, outside stream capture
 cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages);
+
+// Raises a kernel's dynamic shared-memory cap to everything the device allows next to the kernel's
+// static shared memory (a cap, not a reservation), once per kernel, outside stream capture.
+inline cudaError_t raise_smem_cap(const void* fn) {
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, fn);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+}
 
 // cudaLaunchKernelEx with the programmatic-stream-serialization attribute when `pdl` is set, so the
 // kernel may begin while the previous kernel in the stream is still running (it must call

@@ -1,0 +1,149 @@
+"""Isolated decode-kernel benchmark (benchmark config 4; the counterpart of yalm's
+`build/test -bk {matmul,matmul-wide,mha,ffn}`, src/test.cpp:339-405).
+
+    python -m yalm_b200.kbench [--kernel gemv|gateup|qkv|attention|all] [--iters N] [--quick]
+
+Each launch goes through the C ABI (yb_gemv_dev, yb_gateup_dev, yb_qkv_dev, yb_attention_dev) on
+seeded inputs: W ~ N(0, 0.02) fp16, x ~ N(0, 1), q/K/V ~ N(0, 1) fp16.  Launches rotate over enough
+distinct weight / cache copies to cover at least 4x the 126 MB L2, so every launch streams from HBM.
+Time is measured with CUDA events around `iters` back-to-back launches on one stream; GB/s counts
+algorithmic bytes (weights + activations in/out; for attention K + V + q + out).  Prints one JSON
+line per case.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+
+import numpy as np
+
+from . import _lib
+
+L2_BYTES = 126 * 2 ** 20
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _copies(nbytes):
+    return max(1, math.ceil(4 * L2_BYTES / nbytes))
+
+
+def _time(fn, iters, warm=3):
+    import torch
+    for i in range(warm):
+        fn(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(iters):
+        fn(i)
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def bench_gemv(rows, cols, iters, kind="gemv", seed=0):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    wbytes = rows * cols * 2
+    n = _copies(wbytes)
+    ws = [(torch.randn(rows, cols, device="cuda", generator=g) * 0.02).half() for _ in range(n)]
+    x = torch.randn(cols, device="cuda", generator=g)
+    nw = torch.ones(cols, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if kind == "gateup":
+        out = torch.zeros(rows // 2, device="cuda")
+
+        def fn(i):
+            _lib.call("yb_gateup_dev", _p(out), _p(x), _p(ws[i % n]), rows // 2, cols, _p(nw), 1e-5, 1, stream)
+        ybytes = rows // 2 * 4
+    else:
+        out = torch.zeros(rows, device="cuda")
+
+        def fn(i):
+            _lib.call("yb_gemv_dev", _p(out), _p(x), _p(ws[i % n]), rows, cols, None, 0.0, 0, stream)
+        ybytes = rows * 4
+    ms = _time(fn, iters)
+    nbytes = wbytes + cols * 4 + ybytes
+    return {"kernel": kind, "rows": rows, "cols": cols, "us": round(ms * 1000, 2),
+            "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
+
+
+def bench_qkv(dim, nh, nkv, hd, msl, iters, seed=0):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    rows = (nh + 2 * nkv) * hd
+    wbytes = rows * dim * 2
+    n = _copies(wbytes)
+    ws = [(torch.randn(rows, dim, device="cuda", generator=g) * 0.02).half() for _ in range(n)]
+    x = torch.randn(dim, device="cuda", generator=g)
+    nw = torch.ones(dim, device="cuda")
+    q = torch.zeros(nh * hd, device="cuda")
+    kc = torch.zeros(nkv, msl, hd, device="cuda", dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    inv = torch.tensor([1.0 / (1e6 ** (j / hd)) for j in range(0, hd, 2)], device="cuda", dtype=torch.float32)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def fn(i):
+        pos = i % msl
+        _lib.call("yb_qkv_dev", _p(q), _p(kc), _p(vc), _p(x), _p(ws[i % n]), _p(nw), 1e-5, dim, nh, nkv, hd, hd, msl,
+                  pos, pos, 0, 3.0e38, _p(inv), stream)
+    ms = _time(fn, iters)
+    nbytes = wbytes + dim * 8 + nh * hd * 4 + 2 * nkv * hd * 2
+    return {"kernel": "qkv+rope+kv_append", "rows": rows, "cols": dim, "us": round(ms * 1000, 2),
+            "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
+
+
+def bench_attention(nh, nkv, hd, kv_len, iters, seed=0):
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    msl = kv_len
+    kvbytes = 2 * nkv * msl * hd * 2
+    n = _copies(kvbytes)
+    ks = [torch.randn(nkv, msl, hd, device="cuda", generator=g).half() for _ in range(n)]
+    vs = [torch.randn(nkv, msl, hd, device="cuda", generator=g).half() for _ in range(n)]
+    q = torch.randn(nh * hd, device="cuda", generator=g)
+    out = torch.zeros(nh * hd, device="cuda")
+    scratch = torch.zeros(_lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl), dtype=torch.uint8, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def fn(i):
+        _lib.call("yb_attention_dev", _p(out), _p(q), _p(ks[i % n]), _p(vs[i % n]), nh, nkv, hd, msl, kv_len,
+                  _p(scratch), stream)
+    ms = _time(fn, iters)
+    nbytes = kvbytes + 2 * nh * hd * 4
+    return {"kernel": "attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "kv_len": kv_len,
+            "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default="all", choices=["gemv", "gateup", "qkv", "attention", "all"])
+    ap.add_argument("--iters", type=int, default=200)
+    ap.add_argument("--quick", action="store_true", help="one shape per kernel (for profiler captures)")
+    args = ap.parse_args(argv)
+    import torch
+    torch.cuda.set_device(0)
+    rows = []
+    if args.kernel in ("gemv", "all"):
+        shapes = [(32000, 4096)] if args.quick else [(4096, 4096), (4096, 14336), (32000, 4096), (6144, 4096)]
+        for r, c in shapes:
+            rows.append(bench_gemv(r, c, args.iters))
+    if args.kernel in ("gateup", "all"):
+        rows.append(bench_gemv(2 * 14336, 4096, args.iters, kind="gateup"))
+    if args.kernel in ("qkv", "all"):
+        rows.append(bench_qkv(4096, 32, 8, 128, 4096, args.iters))
+    if args.kernel in ("attention", "all"):
+        lens = [4096] if args.quick else [128, 1024, 4096, 16384, 32768]
+        for kv in lens:
+            rows.append(bench_attention(32, 8, 128, kv, args.iters))
+    for r in rows:
+        print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()
