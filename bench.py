@@ -285,8 +285,22 @@ def main():
     step_bytes = c.weight_bytes_per_token(world) + c.kv_bytes_per_token(int(round(kv_mean)), world) + \
         c.n_layers * 2 * (c.n_kv_heads // world) * c.head_dim * 2
     step_gbs = step_bytes / (ms_dev / args.steps / 1000.0) / 1e9
+    executor = m.executor()
     roofline = None
     kernels = {}
+    if executor == "persistent":
+        # the persistent kernel is the whole step: one launch per token
+        achieved = step_bytes / (ms_dev / args.steps / 1000.0) / 1e9
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                traffic = json.load(f).get(f"{args.config}:persistent_step")
+        except Exception:
+            traffic = None
+        roofline = {"bound": "hbm", "kernel": "persistent_step_kernel (one cooperative launch per decode step)",
+                    "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
+                    "fallback 6650 GB/s", "traffic": traffic, "algorithmic_bytes_per_launch": step_bytes}
     if world == 1 and not args.no_profile:
         names = ["qkv", "attention", "wo", "gateup", "w2", "classifier"]
         hid, dim = c.hidden_dim, c.dim
@@ -303,19 +317,20 @@ def main():
             kernels[nm] = {"us": round(msv.value * 1000, 2)}
             if nm in kbytes:
                 kernels[nm]["gbs"] = round(kbytes[nm] / (msv.value / 1000) / 1e9, 1)
-        dom = "gateup"
-        achieved = kernels[dom]["gbs"]
-        traffic = None
-        try:
-            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-                traffic = json.load(f).get(f"{args.config}:{dom}")
-        except Exception:
+        if executor == "graph":
+            dom = "gateup"
+            achieved = kernels[dom]["gbs"]
             traffic = None
-        roofline = {"bound": "hbm", "kernel": f"gemv gate/up (fused W1/W3 + SwiGLU, {2 * hid}x{dim} fp16)",
-                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
-                    "fallback 6650 GB/s", "traffic": traffic,
-                    "algorithmic_bytes_per_launch": kbytes[dom]}
+            try:
+                with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                    traffic = json.load(f).get(f"{args.config}:{dom}")
+            except Exception:
+                traffic = None
+            roofline = {"bound": "hbm", "kernel": f"gemv gate/up (fused W1/W3 + SwiGLU, {2 * hid}x{dim} fp16)",
+                        "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
+                        "fallback 6650 GB/s", "traffic": traffic,
+                        "algorithmic_bytes_per_launch": kbytes[dom]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -329,7 +344,10 @@ def main():
     if world > 1:
         dist.barrier()
     if rank == 0:
-        launches_per_step = 1 + c.n_layers * (4 + m_w2_panels(m)) + 1 + (1 if world > 1 else 0)
+        if executor == "persistent":
+            launches_per_step = 1
+        else:
+            launches_per_step = 1 + c.n_layers * (4 + m_w2_panels(m)) + 1 + (1 if world > 1 else 0)
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_dev / args.steps, 4), "higher_is_better": True,
@@ -345,7 +363,8 @@ def main():
             "roofline": roofline,
             "step_roofline": {"bytes_per_step_per_rank": step_bytes, "achieved_gbs": round(step_gbs, 1), "peak": peak,
                               "frac": round(step_gbs / peak, 4)},
-            "kernels_us": kernels,
+            "executor": executor,
+            "graph_kernels_us": kernels,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,

@@ -107,8 +107,23 @@ void* yb_stream(yb_engine* e);
  * src/infer.cpp:304; this engine keeps both as [kv_head][slot][head_dim]). */
 int yb_read_kv(yb_engine* e, int layer, int kv_head, int slot0, int n, uint16_t* k_out, uint16_t* v_out);
 
+/* Which executor runs the steps: 0 = a CUDA graph of per-phase kernels chained with programmatic
+ * dependent launch (replaces yalm's per-token CUDA graph, src/infer.cu:1296-1378), 1 = one
+ * persistent cooperative kernel per step with bounded grid barriers between phases (replaces
+ * yalm's cooperative kernel_forward, src/coop.cu:179-322).  The graph is the default (it measures
+ * faster on B200); YB_EXECUTOR=persistent selects the persistent kernel when an instantiation exists
+ * for the model shape. */
+int yb_executor(yb_engine* e);
+
+/* Diagnostics for the persistent executor when the engine was created with YB_TRACE=1: copies the
+ * last step's timeline — per CTA (*grid of them) *events %globaltimer stamps in ns: consumer start,
+ * arrive / release of every grid barrier in order, consumer end, producer end (0 = not reached) —
+ * into out (n entries).  out = NULL only reports *grid and *events. */
+int yb_trace_read(yb_engine* e, unsigned long long* out, size_t n, int* grid, int* events);
+
 /* Status word the kernels of the last step wrote (0 = healthy; bit 0 TMA-stage wait timed out,
- * bit 1 tensor-parallel peer wait timed out, bit 2 device-side argument check failed). */
+ * bit 1 tensor-parallel peer wait timed out, bit 2 device-side argument check failed, bit 3 grid
+ * barrier wait timed out). */
 unsigned yb_status(yb_engine* e);
 int yb_clear_status(yb_engine* e);
 

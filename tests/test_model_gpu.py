@@ -17,10 +17,25 @@ def _cos(a, b):
     return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
 
 
-@pytest.fixture(scope="module")
-def tiny_model(gpu, tiny_yalm):
-    y = YALMData(tiny_yalm)
-    m = Model(y).cuda(0)
+def _make(path, executor, context=0):
+    """Engine with the requested executor (yb_create reads YB_EXECUTOR)."""
+    import os
+    old = os.environ.get("YB_EXECUTOR")
+    os.environ["YB_EXECUTOR"] = executor
+    try:
+        m = Model(YALMData(path), context=context).cuda(0)
+    finally:
+        if old is None:
+            del os.environ["YB_EXECUTOR"]
+        else:
+            os.environ["YB_EXECUTOR"] = old
+    assert m.executor() == executor
+    return m
+
+
+@pytest.fixture(scope="module", params=["persistent", "graph"])
+def tiny_model(gpu, tiny_yalm, request):
+    m = _make(tiny_yalm, request.param)
     yield m
     m.close()
 
@@ -84,11 +99,11 @@ def test_kv_cache_matches_reference(tiny_model, golden):
             assert (got != exp).mean() < 0.2
 
 
-def test_ring_buffer_and_sinks_vs_reference(gpu, tiny_yalm):
+@pytest.mark.parametrize("executor", ["persistent", "graph"])
+def test_ring_buffer_and_sinks_vs_reference(gpu, tiny_yalm, executor):
     """Context 48 (yalm -T 48): 120 steps run past max_seq_len, so the cache wraps in ring order
     and the two sink keys are re-rotated every step (src/infer.cpp:307-325, 489-494)."""
-    y = YALMData(tiny_yalm)
-    m = Model(y, context=48).cuda(0)
+    m = _make(tiny_yalm, executor, context=48)
     ref = oracle.RefModel(tiny_yalm, context=48)
     s = InferenceState(m.config)
     rng = np.random.default_rng(9)

@@ -59,6 +59,8 @@ _SIGS = {
     "yb_stream": (_P, [_P]),
     "yb_read_kv": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "yb_status": (ctypes.c_uint, [_P]),
+    "yb_executor": (_I, [_P]),
+    "yb_trace_read": (_I, [_P, _P, _S, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "yb_clear_status": (_I, [_P]),
     "yb_destroy": (None, [_P]),
     "yb_last_error": (_I, [ctypes.c_char_p, _I]),

@@ -26,8 +26,8 @@ NVCC_FLAGS = ARCH + [
     "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC,-O3", "-I" + os.path.join(ROOT, "include"),
 ]
-CU_SOURCES = ["gemv.cu", "attention.cu", "engine.cu", "capi.cu"]
-HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "launch.h", "engine.h"]
+CU_SOURCES = ["gemv.cu", "attention.cu", "persistent.cu", "engine.cu", "capi.cu"]
+HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "persistent.cuh", "launch.h", "engine.h"]
 
 
 def _newer(target: str, deps) -> bool:

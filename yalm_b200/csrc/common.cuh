@@ -119,6 +119,12 @@ __device__ __forceinline__ bool wait_counter_geq(const unsigned* p, unsigned tar
   return true;
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) writes
+// to the same bytes (a ring slot refilled after consumers wrote into it).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- named barrier among consumer warps
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

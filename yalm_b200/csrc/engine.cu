@@ -12,8 +12,10 @@
 // memory and the following matvec adds them up (no separate collective kernel).
 #include "engine.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -202,6 +204,10 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
         a.x_out = x_next;
         x_cur = x_next;
       }
+      if (e->tune.prefetch_wo) {
+        a.pf_src = reinterpret_cast<const unsigned char*>(L.wo);
+        a.pf_bytes = (long long)c.dim * e->q_rows * 2;
+      }
       YB_CK(gemv_launch(e->plan_qkv, a, s, true, pf));
     }
     // ---- attention
@@ -276,6 +282,10 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
           a.peer_counters = e->tp.d_peer_counters + (size_t)pt * e->tp_size;
         } else {
           a.y = x_cur;
+        }
+        if (e->tune.prefetch_qkv && p == panels - 1 && l + 1 < c.n_layers) {
+          a.pf_src = reinterpret_cast<const unsigned char*>(e->layers[l + 1].wqkv);
+          a.pf_bytes = (long long)(e->q_rows + 2 * e->kv_rows) * c.dim * 2;
         }
         YB_CK(gemv_launch(e->plan_w2, a, s, true, pf));
       }
@@ -421,7 +431,60 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
   for (const GemvPlan* p : {&e->plan_qkv, &e->plan_wo, &e->plan_gu, &e->plan_w2, &e->plan_cls})
     YB_CK(gemv_prepare(*p));
   YB_CK(attn_prepare(e->plan_attn));
-  if ((rc = dev_alloc(e, &e->attn_part, e->plan_attn.part_floats * 4))) return rc;
+  // persistent executor: one cooperative kernel per step when an instantiation fits this shape
+  {
+    const char* ex = std::getenv("YB_EXECUTOR");
+    const bool want = ex && std::string(ex) == "persistent";
+    int coop = 0;
+    YB_CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
+    if (want && coop && tp_size == 1) {
+      PersistPlan pp = persist_plan(c.dim, e->q_rows, e->hid, c.head_dim, c.n_heads / c.n_kv_heads, e->n_sms);
+      if (pp.ok) {
+        const int G = pp.grid;
+        int red = 0, max_local = 0;
+        const int shapes[5][2] = {{e->q_rows + 2 * e->kv_rows, pp.rd}, {c.dim, pp.ro}, {2 * e->hid, pp.rd},
+                                  {c.dim, pp.rh}, {e->vocab_l, pp.rd}};
+        for (auto& sh : shapes) {
+          const int ml = persist_max_local(sh[0], sh[1], G, e->tune.persist_static_pct);
+          max_local = std::max(max_local, ml);
+          red = std::max(red, ml * sh[1] * kPWarps);
+        }
+        YB_CK(persist_prepare(pp));
+        int per_sm = 0;
+        const size_t smem = persist_smem_bytes(red, max_local);
+        YB_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pp.fn, kPThreads, smem));
+        if (per_sm >= 1) {
+          e->persistent = true;
+          e->plan_persist = pp;
+          e->persist_red_floats = red;
+          e->persist_max_local = max_local;
+        }
+      }
+    }
+  }
+  if (e->persistent) {
+    std::vector<PLayer> pl(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+      const LayerBuffers& L = e->layers[l];
+      pl[l] = PLayer{L.wqkv, L.wo, L.w13, L.w2, L.rms_att, L.rms_ffn, L.k_cache, L.v_cache};
+    }
+    if ((rc = dev_alloc(e, &e->d_players, pl.size() * sizeof(PLayer)))) return rc;
+    YB_CK(cudaMemcpy(e->d_players, pl.data(), pl.size() * sizeof(PLayer), cudaMemcpyHostToDevice));
+    // barrier counter (8 B), failure flag (4 B), one stage-claim counter per phase (4 B each)
+    e->persist_sync_bytes = (12 + 4 * (5 * (size_t)c.n_layers + 1) * e->tune.persist_claim_ctrs + 15) / 16 * 16;
+    if ((rc = dev_alloc(e, &e->persist_sync, e->persist_sync_bytes))) return rc;
+    YB_CK(cudaMemset(e->persist_sync, 0, e->persist_sync_bytes));
+    const char* tr = std::getenv("YB_TRACE");
+    if (tr && tr[0] == '1') {
+      const size_t n = (size_t)e->plan_persist.grid * kTraceEvents;
+      if ((rc = dev_alloc(e, &e->trace, n * 8))) return rc;
+      YB_CK(cudaMemset(e->trace, 0, n * 8));
+    }
+  }
+  {
+    const size_t pf = std::max(e->plan_attn.part_floats, (size_t)e->nh * kPMaxSplits * (c.head_dim + 2));
+    if ((rc = dev_alloc(e, &e->attn_part, pf * 4))) return rc;
+  }
   if ((rc = dev_alloc(e, &e->attn_cnt, (size_t)e->nkv * 4))) return rc;
   YB_CK(cudaMemset(e->attn_cnt, 0, (size_t)e->nkv * 4));
 
@@ -440,8 +503,10 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
     YB_CK(cudaDeviceSynchronize());
     return 0;
   }
-  if ((rc = build_graph(e, 0))) return rc;
-  if ((rc = build_graph(e, 1))) return rc;
+  if (!e->persistent) {
+    if ((rc = build_graph(e, 0))) return rc;
+    if ((rc = build_graph(e, 1))) return rc;
+  }
   YB_CK(cudaDeviceSynchronize());
   return 0;
 }
@@ -466,10 +531,63 @@ static int launch_step(yb_engine* e, int token, int pos, int mode) {
   if (mode != 0 && mode != 1) return set_error(YB_E_INVALID, "mode must be 0 (hydrate) or 1 (logits)");
   if (token < 0 || token >= e->cfg.vocab_size) return set_error(YB_E_INVALID, "token out of range");
   if (pos < 0) return set_error(YB_E_INVALID, "negative position");
-  if (!e->exec[mode]) return set_error(YB_E_INVALID, "engine not ready (tensor-parallel engines need yb_tp_import)");
+  if (!e->persistent && !e->exec[mode])
+    return set_error(YB_E_INVALID, "engine not ready (tensor-parallel engines need yb_tp_import)");
   YB_CK(cudaSetDevice(e->device));
   e->epoch += 1;
   if (mode == YB_MODE_OUTPUT_LOGITS) e->lepoch += 1;
+  if (e->persistent) {
+    const yb_config& c = e->cfg;
+    PArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.layers = e->d_players;
+    a.n_layers = c.n_layers;
+    a.dim = c.dim;
+    a.q_rows = e->q_rows;
+    a.kv_rows = e->kv_rows;
+    a.hid = e->hid;
+    a.vocab_rows = e->vocab_l;
+    a.head_dim = c.head_dim;
+    a.rotary_dim = c.rotary_dim;
+    a.max_seq_len = c.max_seq_len;
+    a.n_kv = e->nkv;
+    a.eps = c.norm_eps;
+    a.qkv_clip = c.qkv_clip;
+    a.act_silu = c.act;
+    a.emb = e->emb;
+    a.wcls = e->wcls;
+    a.rms_final = e->rms_final;
+    a.inv_freq = e->inv_freq;
+    a.x = e->x;
+    a.x2 = e->x2;
+    a.q = e->q;
+    a.att = e->att;
+    a.hb = e->hb;
+    a.logits = e->logits;
+    a.attn_part = e->attn_part;
+    a.attn_cnt = e->attn_cnt;
+    a.bar = e->persist_sync;
+    a.fail = reinterpret_cast<unsigned*>(e->persist_sync + 1);
+    a.status = e->status_d;
+    a.token = token;
+    a.pos = pos;
+    // src/infer.cpp:489-494
+    a.kv_sink = pos >= c.max_seq_len ? 2 : 0;
+    a.kv_pos = a.kv_sink + (pos - a.kv_sink) % (c.max_seq_len - a.kv_sink);
+    a.kv_len = pos >= c.max_seq_len ? c.max_seq_len : pos + 1;
+    a.mode = mode;
+    a.epoch = e->epoch;
+    a.lepoch = e->lepoch;
+    a.tp_size = 1;
+    a.red_floats = e->persist_red_floats;
+    a.max_local = e->persist_max_local;
+    a.static_pct = e->tune.persist_static_pct;
+    a.claim_ctrs = e->tune.persist_claim_ctrs;
+    a.trace = e->trace;
+    YB_CK(cudaMemsetAsync(e->persist_sync, 0, e->persist_sync_bytes, e->stream));
+    YB_CK(persist_launch(e->plan_persist, a, e->stream));
+    return 0;
+  }
   StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, token, pos, e->cfg.max_seq_len, e->epoch, e->lepoch};
   cudaKernelNodeParams kp = {};
   void* params[] = {&sa};
@@ -487,7 +605,8 @@ static int check_status(yb_engine* e) {
   const unsigned st = *reinterpret_cast<volatile unsigned*>(e->status_h);
   if (st) {
     char buf[160];
-    std::snprintf(buf, sizeof(buf), "device status 0x%x (1: TMA stage wait timed out, 2: peer wait timed out, 4: bad args)", st);
+    std::snprintf(buf, sizeof(buf),
+                  "device status 0x%x (1: TMA stage wait, 2: peer wait, 8: grid barrier wait timed out; 4: bad args)", st);
     return set_error(YB_E_TIMEOUT, buf);
   }
   return 0;
@@ -532,6 +651,21 @@ extern "C" int yb_read_kv(yb_engine* e, int layer, int kv_head, int slot0, int n
   const size_t off = ((size_t)kv_head * e->cfg.max_seq_len + slot0) * hd;
   if (k_out) YB_CK(cudaMemcpy(k_out, e->layers[layer].k_cache + off, (size_t)n * hd * 2, cudaMemcpyDeviceToHost));
   if (v_out) YB_CK(cudaMemcpy(v_out, e->layers[layer].v_cache + off, (size_t)n * hd * 2, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+extern "C" int yb_executor(yb_engine* e) { return e && e->persistent ? 1 : 0; }
+
+extern "C" int yb_trace_read(yb_engine* e, unsigned long long* out, size_t n, int* grid, int* events) {
+  if (!e || !e->persistent || !e->trace) return set_error(YB_E_INVALID, "no timeline (persistent executor with YB_TRACE=1)");
+  const size_t total = (size_t)e->plan_persist.grid * kTraceEvents;
+  if (grid) *grid = e->plan_persist.grid;
+  if (events) *events = kTraceEvents;
+  if (!out) return 0;
+  if (n < total) return set_error(YB_E_INVALID, "timeline buffer too small");
+  YB_CK(cudaSetDevice(e->device));
+  YB_CK(cudaStreamSynchronize(e->stream));
+  YB_CK(cudaMemcpy(out, e->trace, total * 8, cudaMemcpyDeviceToHost));
   return 0;
 }
 

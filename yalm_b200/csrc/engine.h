@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "launch.h"
+#include "persistent.cuh"
 
 namespace yb {
 
@@ -94,6 +95,15 @@ struct yb_engine {
   int w2_panels = 1;
   yb::AttnPlan plan_attn{};
 
+  // executor: per-step CUDA graph of kernels (false) or one persistent cooperative kernel (true)
+  bool persistent = false;
+  yb::PersistPlan plan_persist{};
+  yb::PLayer* d_players = nullptr;
+  unsigned long long* persist_sync = nullptr;  // [0] grid barrier counter, [1] failure flag
+  int persist_red_floats = 0;
+  int persist_max_local = 0;
+  size_t persist_sync_bytes = 0;
+  unsigned long long* trace = nullptr;  // YB_TRACE=1: persistent-kernel timeline of the last step
   cudaGraph_t graph[2] = {nullptr, nullptr};
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
   cudaGraphNode_t step_node[2] = {nullptr, nullptr};

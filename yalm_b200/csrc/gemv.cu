@@ -82,6 +82,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
                    &full[slot], pol);
       }
       issued = i + 1;
+      if (i + 1 == NS && a.pf_src) {
+        // this CTA's share of the L2 warm-up, after its own ring is in flight
+        long long p0 = a.pf_bytes * blockIdx.x / G, p1 = a.pf_bytes * (blockIdx.x + 1) / G;
+        p0 &= ~15ll;
+        p1 = (blockIdx.x + 1 == G) ? a.pf_bytes : (p1 & ~15ll);
+        for (long long o = p0; o < p1; o += 65536) {
+          const long long n = (p1 - o) < 65536 ? (p1 - o) : 65536;
+          bulk_prefetch_l2(a.pf_src + o, (unsigned)n);
+        }
+      }
     }
     // Drain: never leave the CTA while a bulk copy into its shared memory may be in flight.
     for (int i = max(0, issued - NS); i < issued; ++i) mbar_wait(&full[i % NS], (i / NS) & 1, a.status);
@@ -382,6 +392,10 @@ LaunchTuning LaunchTuning::from_env() {
         else if (k == "slots" && v >= 2) t.max_slots = v;
         else if (k == "l2pf" && v >= 0) t.l2_prefetch_stages = v;
         else if (k == "ctas" && v >= 1 && v <= 8) t.ctas_per_sm = v;
+        else if (k == "pstatic" && v >= 0 && v <= 100) t.persist_static_pct = v;
+        else if (k == "pfq" && v >= 0) t.prefetch_qkv = v != 0;
+        else if (k == "pfo" && v >= 0) t.prefetch_wo = v != 0;
+        else if (k == "pctr" && v >= 1 && v <= 64) t.persist_claim_ctrs = v;
       }
       i = j + 1;
     }

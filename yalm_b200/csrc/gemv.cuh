@@ -67,6 +67,10 @@ struct GemvArgs {
   const unsigned* tp_counters;
   int tp_in_grid;
   float* x_out;
+  // optional L2 warm-up of another matrix (the next small matvec's weights), split across CTAs and
+  // issued once after this CTA's ring fill
+  const unsigned char* pf_src;
+  long long pf_bytes;
 };
 
 }  // namespace yb

@@ -237,6 +237,9 @@ class Model:
         _lib.call("yb_read_kv", self.engine, layer, kv_head, slot0, n, k.ctypes.data, v.ctypes.data)
         return k, v
 
+    def executor(self) -> str:
+        return "persistent" if _lib.lib().yb_executor(self.engine) == 1 else "graph"
+
     def status(self) -> int:
         return int(_lib.lib().yb_status(self.engine))
 
