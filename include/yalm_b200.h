@@ -4,7 +4,7 @@
  * The engine replaces the GPU side of yalm's `Model::forward` device dispatch
  * (src/model.cpp:479-494 of the yalm repository): the CUDA-graph backend `_forward_cuda`
  * (src/infer.cu:1274-1378) and the cooperative backend `yalm_coop_prepare` / `yalm_coop_forward`
- * (src/coop.h:5-6).  A yalm build binds it from a small shim (see INTEGRATION.md): the shim fills
+ * (src/coop.h:5-6).  A yalm build binds it from a small shim: the shim fills
  * `yb_config` / `yb_weights` from yalm's `Config` and `Block` host pointers (the mmap'd .yalm
  * tensors, before `Model::cuda()` would upload them) and calls `yb_forward` with
  * `InferenceState::logits()`.
