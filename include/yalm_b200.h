@@ -202,6 +202,26 @@ int yb_attention_dev(float* out, const float* q, const uint16_t* k_cache, const 
                      int n_kv_heads, int head_dim, int max_seq_len, int kv_len, void* scratch_dev, void* stream);
 size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
 
+/* No counterpart in the yalm reference (it allocates with cudaMalloc wherever it needs memory).
+ * yb_attention_dev for callers that must not allocate device memory when they call it — for
+ * example a plugin whose host framework owns all device memory through its own allocator, or a
+ * serving loop that forbids allocation after start-up to keep latency and memory use fixed.  Same
+ * arguments and results as yb_attention_dev, without scratch_dev: the scratch lives in a fixed
+ * YB_ATTENTION_NOALLOC_SCRATCH_BYTES array inside this library's device memory, which every GPU that
+ * loads the library holds until the process exits.  Nothing is allocated or freed by the call.
+ *  - Limit: yb_attention_scratch_bytes(n_heads, n_kv_heads, head_dim, max_seq_len) must not exceed
+ *    YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4 MiB: e.g. 32 heads of 128 at max_seq_len 30720); larger
+ *    shapes return YB_E_INVALID with the sizes in yb_last_error().
+ *  - The first call on each device looks up the array's device address (cudaGetSymbolAddress with
+ *    that device current); make that first call before any stream capture on the device.
+ *  - All calls on a device share the one array, which keeps the previous call's contents (each
+ *    call clears the part that must start at zero).  Calls whose executions overlap on the GPU, on
+ *    different streams or host threads, race on it and give wrong results: order them on one
+ *    stream or synchronise between them. */
+#define YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)
+int yb_attention_dev_noalloc(float* out, const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                             int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int kv_len, void* stream);
+
 /* Number of streaming multiprocessors the kernels size their grids for (device 0 if none set). */
 int yb_num_sms(void);
 
