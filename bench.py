@@ -180,6 +180,7 @@ def main():
     ap.add_argument("--cpu-baseline-steps", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
+    ap.add_argument("--no-long-context", action="store_true", help="skip the config-3 (3202-token prefill) phase")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -332,6 +333,10 @@ def main():
                         "fallback 6650 GB/s", "traffic": traffic,
                         "algorithmic_bytes_per_launch": kbytes[dom]}
 
+    long_ctx = None
+    if args.config == "mistral-7b" and not args.no_long_context:
+        long_ctx = long_context(m, c, args, stream, world, dist, peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         d = cpu_baseline(path, context, args.cpu_baseline_steps)
@@ -366,6 +371,7 @@ def main():
             "executor": executor,
             "graph_kernels_us": kernels,
             "cpu_baseline": cpu,
+            "long_context": long_ctx,
             "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,
         }
@@ -375,6 +381,59 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+LONG_PREFILL, LONG_DECODE = 3202, 30
+
+
+def long_context(m, c, args, stream, world, dist, peak):
+    """a 3202-token random prompt hydrated one token at a time (yalm's
+    prefill, src/main.cpp:171-177), then 30 decode tokens timed with CUDA events on the engine stream
+    (kv_len 3203..3232), plus the attention kernel alone at kv_len 3232 (yb_profile_kernel, one GPU)."""
+    import ctypes
+    import torch
+    from yalm_b200 import InferenceMode, _lib
+    rng = np.random.default_rng(4321)
+    prompt = rng.integers(0, c.vocab_size, LONG_PREFILL)
+    toks = rng.integers(0, c.vocab_size, LONG_DECODE)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for pos, tok in enumerate(prompt):
+        m.forward_async(int(tok), pos, InferenceMode.HYDRATE_KV_CACHE if pos + 1 < LONG_PREFILL else InferenceMode.OUTPUT_LOGITS)
+    m.sync()
+    t_prefill = time.perf_counter() - t0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i, tok in enumerate(toks):
+        m.forward_async(int(tok), LONG_PREFILL + i)
+    ev1.record(stream)
+    ev1.synchronize()
+    m.sync()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    kv_mean = LONG_PREFILL + (LONG_DECODE + 1) / 2.0
+    step_bytes = c.weight_bytes_per_token(world) + c.kv_bytes_per_token(int(round(kv_mean)), world)
+    out = {"workload": f"{LONG_PREFILL}-token random prompt (HYDRATE), then {LONG_DECODE} decode tokens, "
+                       f"kv_len {LONG_PREFILL + 1}..{LONG_PREFILL + LONG_DECODE}",
+           "decode_tok_s": round(LONG_DECODE / (ms / 1000.0), 3), "ms_per_step": round(ms / LONG_DECODE, 4),
+           "prefill_tok_s_one_token_steps": round(LONG_PREFILL / t_prefill, 1),
+           "step_roofline": {"bytes_per_step_per_rank": step_bytes,
+                             "achieved_gbs": round(step_bytes / (ms / LONG_DECODE / 1000.0) / 1e9, 1),
+                             "frac": round(step_bytes / (ms / LONG_DECODE / 1000.0) / 1e9 / peak, 4)}}
+    if world == 1 and not args.no_profile:
+        msv = ctypes.c_float()
+        _lib.call("yb_profile_kernel", m.engine, 1, c.n_layers * 4, ctypes.byref(msv))
+        kv_len = LONG_PREFILL + LONG_DECODE
+        abytes = 2 * c.n_kv_heads * c.head_dim * 2 * kv_len + 2 * c.n_heads * c.head_dim * 4
+        out["attention"] = {"kv_len": kv_len, "us": round(msv.value * 1000, 2),
+                            "gbs": round(abytes / (msv.value / 1000) / 1e9, 1), "bytes": abytes}
+    return out
 
 
 def m_w2_panels(m) -> int:

@@ -115,10 +115,17 @@ int yb_read_kv(yb_engine* e, int layer, int kv_head, int slot0, int n, uint16_t*
  * for the model shape. */
 int yb_executor(yb_engine* e);
 
-/* Diagnostics for the persistent executor when the engine was created with YB_TRACE=1: copies the
- * last step's timeline — per CTA (*grid of them) *events %globaltimer stamps in ns: consumer start,
- * arrive / release of every grid barrier in order, consumer end, producer end (0 = not reached) —
- * into out (n entries).  out = NULL only reports *grid and *events. */
+/* Diagnostics for an engine created with YB_TRACE=1: copies the last step's timeline, *grid rows
+ * (CTAs) of *events %globaltimer stamps in ns (0 = not reached), into out (n entries); out = NULL
+ * only reports *grid and *events.
+ *  - persistent executor: per CTA, consumer start, arrive / release of every grid barrier in order,
+ *    consumer end, producer end.
+ *  - graph executor: 8 stamps per kernel of the step in launch order (per layer qkv, attention, wo,
+ *    gate/up, w2; then the classifier in logits mode): for the matvecs j = 0 entry, 1 input vector
+ *    loaded, 2 tensor-parallel partial sums added, 3 last weight stage consumed, 4 epilogue done;
+ *    for attention (row = blockIdx.y * gridDim.x + blockIdx.x) 0 entry, 1 inputs ready, 2 first
+ *    K/V sub-chunk staged, 5 scores done, 6 V pass done, 3 slice done, 4 exit.  Rows beyond a
+ *    kernel's grid stay 0. */
 int yb_trace_read(yb_engine* e, unsigned long long* out, size_t n, int* grid, int* events);
 
 /* Status word the kernels of the last step wrote (0 = healthy; bit 0 TMA-stage wait timed out,

@@ -15,12 +15,18 @@ struct AttnArgs {
   const __half* k_cache;  // [n_kv_heads][max_seq_len][head_dim]
   const __half* v_cache;  // [n_kv_heads][max_seq_len][head_dim]
   float* out;             // [n_heads][head_dim]
-  float* part;            // [n_heads][s_max][head_dim + 2] slice partials (o, m, l)
+  float* part;            // [n_heads][s_max][head_dim + 4] slice partials (o, m, l, padding)
   unsigned* counters;     // [n_kv_heads], zero between launches
   const StepState* step;  // kv_len is read from here when non-null ...
   int kv_len;             // ... else from here
   int max_seq_len;
   unsigned* status;
+  // optional timeline (null = off): per CTA c = blockIdx.y * gridDim.x + blockIdx.x,
+  // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 1 inputs ready, 2 first K/V
+  // sub-chunk staged, 5 scores done, 6 V pass done (thread 0), 3 slice partial written, 4 exit
+  // (inactive slices stamp only 0 and 1)
+  unsigned long long* trace;
+  int trace_stride;
 };
 
 struct AttnPlan {
@@ -31,6 +37,22 @@ struct AttnPlan {
   size_t smem;
   size_t part_floats;
 };
+
+// Shared memory of one attention CTA before the score buffer: the K/V stage, or, when larger and
+// below kAttnMergeSmemMax, the slice partials of one kv head (merged in shared memory).
+constexpr size_t kAttnMergeSmemMax = 96 * 1024;
+__host__ __device__ constexpr size_t attn_stage_bytes(int hd) { return (size_t)2 * 2 * 64 * hd * 2; }
+__host__ __device__ constexpr size_t attn_merge_bytes(int hd, int gq, int s_max) {
+  return (size_t)gq * s_max * (hd + 4) * 4 + (size_t)2 * gq * s_max * 4;
+}
+__host__ __device__ constexpr bool attn_merge_in_smem(int hd, int gq, int s_max) {
+  return attn_merge_bytes(hd, gq, s_max) <= kAttnMergeSmemMax;
+}
+__host__ __device__ constexpr size_t attn_region_bytes(int hd, int gq, int s_max) {
+  return attn_merge_in_smem(hd, gq, s_max) && attn_merge_bytes(hd, gq, s_max) > attn_stage_bytes(hd)
+             ? (attn_merge_bytes(hd, gq, s_max) + 127) / 128 * 128
+             : attn_stage_bytes(hd);
+}
 
 AttnPlan attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
 cudaError_t attn_prepare(const AttnPlan& p);  // once per plan, outside stream capture

@@ -105,6 +105,31 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Adds v to *p (possibly another GPU's memory) with release semantics at system scope.  Issued by
+// one thread after a CTA barrier, it publishes every write the CTA made before the barrier (the
+// release is cumulative over writes ordered before it by the barrier), so only that thread pays
+// for the system-scope fence.
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Stores one 8-byte exchange word {lo: fp32 bits, hi: epoch} (possibly into another GPU's memory);
+// the word is written as a unit, so a reader that sees the epoch also sees the value.
+__device__ __forceinline__ void st_ll(unsigned long long* p, float v, unsigned epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// Loads the 8 exchange words at p (16-byte aligned, 4 independent 16-byte loads).
+__device__ __forceinline__ void ll_load8(const unsigned long long* p, unsigned long long* w) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w[2 * i]), "=l"(w[2 * i + 1]) : "l"(p + 2 * i) : "memory");
+}
+__device__ __forceinline__ bool ll_ready8(const unsigned long long* w, unsigned epoch) {
+  bool all = true;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) all = all && (unsigned)(w[i] >> 32) == epoch;
+  return all;
+}
 // Waits until *p >= target (wrap-safe); false + kStatusPeerTimeout when the budget runs out.
 __device__ __forceinline__ bool wait_counter_geq(const unsigned* p, unsigned target, unsigned* status) {
   if ((int)(ld_acquire_sys(p) - target) >= 0) return true;
@@ -126,6 +151,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ---------------------------------------------------------------- named barrier among consumer warps
+// %globaltimer in ns (timeline diagnostics).
+__device__ __forceinline__ unsigned long long timeline_ns() {
+  unsigned long long v;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(v));
+  return v;
+}
+// Per-CTA timeline stamp j of one kernel launch: trace[blockIdx.x * stride + j] (trace null = off).
+__device__ __forceinline__ void timeline_stamp(unsigned long long* trace, int stride, int j) {
+  if (trace) trace[(size_t)blockIdx.x * stride + j] = timeline_ns();
+}
+
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

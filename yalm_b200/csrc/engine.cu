@@ -153,6 +153,12 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
   return 0;
 }
 
+// This rank's exchange words of point pt (all ranks' partials, [tp][dim]).
+static const unsigned long long* tp_in(yb_engine* e, int pt) {
+  return reinterpret_cast<const unsigned long long*>(static_cast<char*>(e->tp.base) + e->tp.x_off) +
+         (size_t)pt * e->tp_size * e->cfg.dim;
+}
+
 static GemvArgs base_args(yb_engine* e) {
   GemvArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -173,6 +179,12 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
   const bool tp = e->tp_size > 1;
   const int pf = e->tune.l2_prefetch_stages;
   float* x_cur = e->x;  // TP: the residual stream ping-pongs between x and x2
+  int kix = 0;          // kernel index within the step (timeline column block)
+  auto timeline = [&](unsigned long long** tr, int* stride) {
+    *tr = e->gtrace ? e->gtrace + (size_t)kix * 8 : nullptr;
+    *stride = e->gtrace_events;
+    ++kix;
+  };
   for (int l = 0; l < c.n_layers; ++l) {
     LayerBuffers& L = e->layers[l];
     // ---- QKV
@@ -194,12 +206,10 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       a.inv_freq = e->inv_freq;
       a.k_cache = L.k_cache;
       a.v_cache = L.v_cache;
+      a.kv_prefetch = 1;
       if (tp && l > 0) {
         // add the previous layer's w2 partials (exchange point 2l-1)
-        const int pt = 2 * l - 1;
-        a.tp_slots = reinterpret_cast<const float*>(static_cast<char*>(e->tp.base) + e->tp.x_off) + (size_t)pt * e->tp_size * c.dim;
-        a.tp_counters = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) + (size_t)pt * e->tp_size;
-        a.tp_in_grid = e->plan_w2.grid;
+        a.tp_ll = tp_in(e, 2 * l - 1);
         float* x_next = (x_cur == e->x) ? e->x2 : e->x;
         a.x_out = x_next;
         x_cur = x_next;
@@ -208,7 +218,8 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
         a.pf_src = reinterpret_cast<const unsigned char*>(L.wo);
         a.pf_bytes = (long long)c.dim * e->q_rows * 2;
       }
-      YB_CK(gemv_launch(e->plan_qkv, a, s, true, pf));
+      timeline(&a.trace, &a.trace_stride);
+      YB_CK(gemv_launch(a.tp_ll ? e->plan_qkv_tp : e->plan_qkv, a, s, true, pf));
     }
     // ---- attention
     {
@@ -223,6 +234,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       a.step = e->step;
       a.max_seq_len = c.max_seq_len;
       a.status = e->status_d;
+      timeline(&a.trace, &a.trace_stride);
       YB_CK(attn_launch(e->plan_attn, a, s, true));
     }
     // ---- wo (+ residual, or partials to peers)
@@ -234,13 +246,11 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       a.cols = e->q_rows;
       a.x = e->att;
       if (tp) {
-        const int pt = 2 * l;
-        a.peer_slots = e->tp.d_peer_slots + (size_t)pt * e->tp_size;
-        a.peer_counters = e->tp.d_peer_counters + (size_t)pt * e->tp_size;
-        a.row_offset = 0;
+        a.peer_ll = e->tp.d_peer_ll + (size_t)(2 * l) * e->tp_size;
       } else {
         a.y = x_cur;
       }
+      timeline(&a.trace, &a.trace_stride);
       YB_CK(gemv_launch(e->plan_wo, a, s, true, pf));
     }
     // ---- gate/up (+ RMSNorm, SwiGLU)
@@ -255,14 +265,12 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       a.y = e->hb;
       a.act_silu = c.act;
       if (tp) {
-        const int pt = 2 * l;
-        a.tp_slots = reinterpret_cast<const float*>(static_cast<char*>(e->tp.base) + e->tp.x_off) + (size_t)pt * e->tp_size * c.dim;
-        a.tp_counters = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) + (size_t)pt * e->tp_size;
-        a.tp_in_grid = e->plan_wo.grid;
+        a.tp_ll = tp_in(e, 2 * l);
         float* x_next = (x_cur == e->x) ? e->x2 : e->x;
         a.x_out = x_next;
         x_cur = x_next;
       }
+      timeline(&a.trace, &a.trace_stride);
       YB_CK(gemv_launch(e->plan_gu, a, s, true, pf));
     }
     // ---- w2 (+ residual, or partials to peers); column panels when hidden_l > 14336
@@ -277,9 +285,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
         a.cols = pcols;
         a.x = e->hb + (size_t)p * pcols;
         if (tp) {
-          const int pt = 2 * l + 1;
-          a.peer_slots = e->tp.d_peer_slots + (size_t)pt * e->tp_size;
-          a.peer_counters = e->tp.d_peer_counters + (size_t)pt * e->tp_size;
+          a.peer_ll = e->tp.d_peer_ll + (size_t)(2 * l + 1) * e->tp_size;
         } else {
           a.y = x_cur;
         }
@@ -287,6 +293,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
           a.pf_src = reinterpret_cast<const unsigned char*>(e->layers[l + 1].wqkv);
           a.pf_bytes = (long long)(e->q_rows + 2 * e->kv_rows) * c.dim * 2;
         }
+        timeline(&a.trace, &a.trace_stride);
         YB_CK(gemv_launch(e->plan_w2, a, s, true, pf));
       }
     }
@@ -300,21 +307,17 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
     a.x = x_cur;
     a.norm_w = e->rms_final;
     if (tp) {
-      const int pt = 2 * c.n_layers - 1;
-      a.tp_slots = reinterpret_cast<const float*>(static_cast<char*>(e->tp.base) + e->tp.x_off) + (size_t)pt * e->tp_size * c.dim;
-      a.tp_counters = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) + (size_t)pt * e->tp_size;
-      a.tp_in_grid = e->plan_w2.grid;
-      const int gp = 2 * c.n_layers;  // gather point
-      a.peer_slots = e->tp.d_peer_slots + (size_t)gp * e->tp_size;
-      a.peer_counters = e->tp.d_peer_counters + (size_t)gp * e->tp_size;
+      a.tp_ll = tp_in(e, 2 * c.n_layers - 1);
+      a.peer_slots = e->tp.d_peer_slots;
+      a.peer_counters = e->tp.d_peer_counters;
       a.row_offset = e->tp_rank * e->vocab_l;
     } else {
       a.y = e->logits;
     }
+    timeline(&a.trace, &a.trace_stride);
     YB_CK(gemv_launch(e->plan_cls, a, s, true, pf));
     if (tp) {
-      const unsigned* cnt = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off) +
-                            (size_t)(2 * c.n_layers) * e->tp_size;
+      const unsigned* cnt = reinterpret_cast<const unsigned*>(static_cast<char*>(e->tp.base) + e->tp.cnt_off);
       struct {
         const StepState* step;
         const unsigned* counters;
@@ -417,18 +420,21 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
   const int epi_res = tp_size > 1 ? kEpiResidTP : kEpiResid;
   e->plan_qkv = gemv_plan(e->q_rows + 2 * e->kv_rows, c.dim, kEpiQKV, true, e->n_sms, e->tune);
   e->plan_wo = gemv_plan(c.dim, e->q_rows, epi_res, false, e->n_sms, e->tune);
-  e->plan_gu = gemv_plan(2 * e->hid, c.dim, kEpiGateUp, true, e->n_sms, e->tune);
+  e->plan_gu = gemv_plan(2 * e->hid, c.dim, kEpiGateUp, true, e->n_sms, e->tune, tp_size > 1);
+  e->plan_qkv_tp = tp_size > 1 ? gemv_plan(e->q_rows + 2 * e->kv_rows, c.dim, kEpiQKV, true, e->n_sms, e->tune, true)
+                               : e->plan_qkv;
   e->w2_panels = 1;
   while (gemv_kpt_for(e->hid / e->w2_panels) < 0 || (e->hid / e->w2_panels) % 8 || e->hid % e->w2_panels) {
     if (++e->w2_panels > 16) return set_error(YB_E_UNSUPPORTED, "hidden_dim too large");
   }
   if (tp_size > 1 && e->w2_panels > 1) return set_error(YB_E_UNSUPPORTED, "hidden_dim per rank too large for tensor parallelism");
   e->plan_w2 = gemv_plan(c.dim, e->hid / e->w2_panels, epi_res, false, e->n_sms, e->tune);
-  e->plan_cls = gemv_plan(e->vocab_l, c.dim, tp_size > 1 ? kEpiStoreTP : kEpiStore, true, e->n_sms, e->tune);
+  e->plan_cls = gemv_plan(e->vocab_l, c.dim, tp_size > 1 ? kEpiStoreTP : kEpiStore, true, e->n_sms, e->tune, tp_size > 1);
   e->plan_attn = attn_plan(e->nh, e->nkv, c.head_dim, c.max_seq_len);
-  if (!e->plan_qkv.ok || !e->plan_wo.ok || !e->plan_gu.ok || !e->plan_w2.ok || !e->plan_cls.ok || !e->plan_attn.ok)
+  if (!e->plan_qkv.ok || !e->plan_qkv_tp.ok || !e->plan_wo.ok || !e->plan_gu.ok || !e->plan_w2.ok ||
+      !e->plan_cls.ok || !e->plan_attn.ok)
     return set_error(YB_E_UNSUPPORTED, "no kernel configuration for this model shape");
-  for (const GemvPlan* p : {&e->plan_qkv, &e->plan_wo, &e->plan_gu, &e->plan_w2, &e->plan_cls})
+  for (const GemvPlan* p : {&e->plan_qkv, &e->plan_qkv_tp, &e->plan_wo, &e->plan_gu, &e->plan_w2, &e->plan_cls})
     YB_CK(gemv_prepare(*p));
   YB_CK(attn_prepare(e->plan_attn));
   // persistent executor: one cooperative kernel per step when an instantiation fits this shape
@@ -487,15 +493,29 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
   }
   if ((rc = dev_alloc(e, &e->attn_cnt, (size_t)e->nkv * 4))) return rc;
   YB_CK(cudaMemset(e->attn_cnt, 0, (size_t)e->nkv * 4));
+  if (!e->persistent) {
+    const char* tr = std::getenv("YB_TRACE");
+    if (tr && tr[0] == '1') {
+      int rows = (int)(e->plan_attn.grid.x * e->plan_attn.grid.y);
+      for (const GemvPlan* p : {&e->plan_qkv, &e->plan_wo, &e->plan_gu, &e->plan_w2, &e->plan_cls})
+        rows = std::max(rows, p->grid);
+      const int n_kern = c.n_layers * (4 + e->w2_panels) + 1;
+      e->gtrace_rows = rows;
+      e->gtrace_events = n_kern * 8;
+      const size_t n = (size_t)rows * e->gtrace_events;
+      if ((rc = dev_alloc(e, &e->gtrace, n * 8))) return rc;
+      YB_CK(cudaMemset(e->gtrace, 0, n * 8));
+    }
+  }
 
   if (tp_size > 1) {
     // exchange region: partial-sum slots, gathered logits, arrival counters
     TpRegion& t = e->tp;
     const size_t n_pts = 2 * (size_t)c.n_layers;
     t.x_off = 0;
-    t.logit_off = n_pts * tp_size * c.dim * 4;
+    t.logit_off = n_pts * tp_size * c.dim * 8;
     t.cnt_off = t.logit_off + (size_t)c.vocab_size * 4;
-    t.bytes = t.cnt_off + (n_pts + 1) * tp_size * 4;
+    t.bytes = t.cnt_off + (size_t)tp_size * 4;
     t.bytes = (t.bytes + 4095) / 4096 * 4096;
     YB_CK(cudaMalloc(&t.base, t.bytes));
     YB_CK(cudaMemset(t.base, 0, t.bytes));
@@ -657,7 +677,18 @@ extern "C" int yb_read_kv(yb_engine* e, int layer, int kv_head, int slot0, int n
 extern "C" int yb_executor(yb_engine* e) { return e && e->persistent ? 1 : 0; }
 
 extern "C" int yb_trace_read(yb_engine* e, unsigned long long* out, size_t n, int* grid, int* events) {
-  if (!e || !e->persistent || !e->trace) return set_error(YB_E_INVALID, "no timeline (persistent executor with YB_TRACE=1)");
+  if (e && !e->persistent && e->gtrace) {
+    const size_t total = (size_t)e->gtrace_rows * e->gtrace_events;
+    if (grid) *grid = e->gtrace_rows;
+    if (events) *events = e->gtrace_events;
+    if (!out) return 0;
+    if (n < total) return set_error(YB_E_INVALID, "timeline buffer too small");
+    YB_CK(cudaSetDevice(e->device));
+    YB_CK(cudaStreamSynchronize(e->stream));
+    YB_CK(cudaMemcpy(out, e->gtrace, total * 8, cudaMemcpyDeviceToHost));
+    return 0;
+  }
+  if (!e || !e->persistent || !e->trace) return set_error(YB_E_INVALID, "no timeline (engine created without YB_TRACE=1)");
   const size_t total = (size_t)e->plan_persist.grid * kTraceEvents;
   if (grid) *grid = e->plan_persist.grid;
   if (events) *events = kTraceEvents;
@@ -687,6 +718,7 @@ extern "C" void yb_destroy(yb_engine* e) {
   }
   for (size_t i = 0; i < e->tp.peer_base.size(); ++i)
     if ((int)i != e->tp_rank && e->tp.peer_base[i]) cudaIpcCloseMemHandle(e->tp.peer_base[i]);
+  if (e->tp.d_peer_ll) cudaFree(e->tp.d_peer_ll);
   if (e->tp.d_peer_slots) cudaFree(e->tp.d_peer_slots);
   if (e->tp.d_peer_counters) cudaFree(e->tp.d_peer_counters);
   if (e->tp.base) cudaFree(e->tp.base);
@@ -829,26 +861,26 @@ extern "C" int yb_tp_import(yb_engine* e, const void* blobs, size_t stride) {
       e->tp.peer_base[r] = p;
     }
   }
-  // Destinations: at exchange point pt, rank `me` writes its partial into rank p's slot
-  // [pt][me][:] and bumps rank p's counter [pt][me].  Point 2L is the logits gather.
-  const int n_pts = 2 * c.n_layers + 1;
-  std::vector<float*> slots((size_t)n_pts * P);
-  std::vector<unsigned*> cnts((size_t)n_pts * P);
-  for (int pt = 0; pt < n_pts; ++pt) {
-    for (int p = 0; p < P; ++p) {
-      char* base = static_cast<char*>(e->tp.peer_base[p]);
-      float* dst;
-      if (pt < 2 * c.n_layers)
-        dst = reinterpret_cast<float*>(base + e->tp.x_off) + ((size_t)pt * P + e->tp_rank) * c.dim;
-      else
-        dst = reinterpret_cast<float*>(base + e->tp.logit_off);
-      slots[(size_t)pt * P + p] = dst;
-      cnts[(size_t)pt * P + p] = reinterpret_cast<unsigned*>(base + e->tp.cnt_off) + (size_t)pt * P + e->tp_rank;
-    }
+  // Destinations: at exchange point pt < 2L, rank `me` writes its partial words into rank p's
+  // slot [pt][me][:]; the classifier writes its vocabulary rows into every rank's logits buffer and
+  // bumps that rank's counter [me].
+  const int n_pts = 2 * c.n_layers;
+  std::vector<unsigned long long*> ll((size_t)n_pts * P);
+  std::vector<float*> lg(P);
+  std::vector<unsigned*> cnts(P);
+  for (int p = 0; p < P; ++p) {
+    char* base = static_cast<char*>(e->tp.peer_base[p]);
+    for (int pt = 0; pt < n_pts; ++pt)
+      ll[(size_t)pt * P + p] =
+          reinterpret_cast<unsigned long long*>(base + e->tp.x_off) + ((size_t)pt * P + e->tp_rank) * c.dim;
+    lg[p] = reinterpret_cast<float*>(base + e->tp.logit_off);
+    cnts[p] = reinterpret_cast<unsigned*>(base + e->tp.cnt_off) + e->tp_rank;
   }
-  YB_CK(cudaMalloc(&e->tp.d_peer_slots, slots.size() * sizeof(float*)));
+  YB_CK(cudaMalloc(&e->tp.d_peer_ll, ll.size() * sizeof(unsigned long long*)));
+  YB_CK(cudaMalloc(&e->tp.d_peer_slots, lg.size() * sizeof(float*)));
   YB_CK(cudaMalloc(&e->tp.d_peer_counters, cnts.size() * sizeof(unsigned*)));
-  YB_CK(cudaMemcpy(e->tp.d_peer_slots, slots.data(), slots.size() * sizeof(float*), cudaMemcpyHostToDevice));
+  YB_CK(cudaMemcpy(e->tp.d_peer_ll, ll.data(), ll.size() * sizeof(unsigned long long*), cudaMemcpyHostToDevice));
+  YB_CK(cudaMemcpy(e->tp.d_peer_slots, lg.data(), lg.size() * sizeof(float*), cudaMemcpyHostToDevice));
   YB_CK(cudaMemcpy(e->tp.d_peer_counters, cnts.data(), cnts.size() * sizeof(unsigned*), cudaMemcpyHostToDevice));
   e->tp.joined = true;
   int rc;

@@ -40,11 +40,14 @@ struct LayerBuffers {
 struct TpRegion {
   void* base = nullptr;          // local allocation
   size_t bytes = 0;
-  size_t x_off = 0;              // [2*n_layers][tp][dim] fp32 partial slots
+  size_t x_off = 0;              // [2*n_layers][tp][dim] exchange words {fp32 partial, epoch}
   size_t logit_off = 0;          // [vocab] fp32 gathered logits
-  size_t cnt_off = 0;            // [2*n_layers + 1][tp] u32 arrival counters
+  size_t cnt_off = 0;            // [tp] u32 logits arrival counters
   std::vector<void*> peer_base;  // per rank (own rank: base)
-  float** d_peer_slots = nullptr;      // device arrays of pointers used by kernels
+  // device arrays of pointers used by kernels: [2*n_layers][tp] exchange destinations, [tp]
+  // logits destinations and counters
+  unsigned long long** d_peer_ll = nullptr;
+  float** d_peer_slots = nullptr;
   unsigned** d_peer_counters = nullptr;
   bool joined = false;
 };
@@ -92,6 +95,7 @@ struct yb_engine {
 
   yb::LaunchTuning tune;
   yb::GemvPlan plan_qkv{}, plan_wo{}, plan_gu{}, plan_w2{}, plan_cls{};
+  yb::GemvPlan plan_qkv_tp{};  // tensor parallel: QKV of layers >= 1 (adds the previous w2 partials)
   int w2_panels = 1;
   yb::AttnPlan plan_attn{};
 
@@ -104,6 +108,10 @@ struct yb_engine {
   int persist_max_local = 0;
   size_t persist_sync_bytes = 0;
   unsigned long long* trace = nullptr;  // YB_TRACE=1: persistent-kernel timeline of the last step
+  // YB_TRACE=1 with the graph executor: per kernel of the step (in launch order: per layer qkv,
+  // attention, wo, gate/up, w2 panels; then the classifier) 8 stamps per CTA, [cta][kernel * 8 + j]
+  unsigned long long* gtrace = nullptr;
+  int gtrace_rows = 0, gtrace_events = 0;
   cudaGraph_t graph[2] = {nullptr, nullptr};
   cudaGraphExec_t exec[2] = {nullptr, nullptr};
   cudaGraphNode_t step_node[2] = {nullptr, nullptr};

@@ -8,14 +8,20 @@
 
 namespace yb {
 
-template <int NW, int KPT, int RT, int EPI, bool NORM>
+// IN: 0 = x as given, 1 = RMS-normalised x, 2 = RMS-normalised x plus the tensor-parallel partial
+// sums of the previous row-parallel matvec (GemvArgs::tp_ll).  Only IN == 2 instances carry the
+// exchange-read code, so the others keep their registers for the stream loop.
+template <int NW, int KPT, int RT, int EPI, int IN>
 __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a) {
+  constexpr bool NORM = IN >= 1;
+  constexpr bool TPIN = IN == 2;
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   constexpr int NT = NW * 32;  // consumer threads
 
   pdl_trigger();
+  if (threadIdx.x == 0) timeline_stamp(a.trace, a.trace_stride, 0);
 
   const int T = (a.rows + RT - 1) / RT;  // stages over the whole matrix
   const int G = gridDim.x;
@@ -82,6 +88,25 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
                    &full[slot], pol);
       }
       issued = i + 1;
+      if (EPI == kEpiQKV && a.kv_prefetch && a.step && i + 1 == min(NS, n_st)) {
+        // this CTA's share of the K/V cache rows the attention kernel will read; the step state
+        // may still be the previous step's (a prefetch only)
+        int hl = *reinterpret_cast<const volatile int*>(&a.step->kv_len);
+        hl = hl < 1 ? 1 : (hl > a.max_seq_len ? a.max_seq_len : hl);
+        const long long per = (long long)hl * a.head_dim * 2;  // bytes per head, K or V
+        const int n_kv = a.kv_rows / a.head_dim;
+        const long long total = 2ll * n_kv * per;
+        long long o = (total * blockIdx.x / G) & ~15ll;
+        const long long end = (blockIdx.x + 1 == G) ? total : ((total * (blockIdx.x + 1) / G) & ~15ll);
+        while (o < end) {
+          const long long seg = o / per, off = o - seg * per;
+          const __half* base = (seg < n_kv ? a.k_cache : a.v_cache) + (size_t)(seg % n_kv) * a.max_seq_len * a.head_dim;
+          long long n = per - off < end - o ? per - off : end - o;
+          if (n > 65536) n = 65536;
+          bulk_prefetch_l2(reinterpret_cast<const unsigned char*>(base) + off, (unsigned)n);
+          o += n;
+        }
+      }
       if (i + 1 == NS && a.pf_src) {
         // this CTA's share of the L2 warm-up, after its own ring is in flight
         long long p0 = a.pf_bytes * blockIdx.x / G, p1 = a.pf_bytes * (blockIdx.x + 1) / G;
@@ -127,31 +152,69 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
       xr[k][1] = xr[k][0];
     }
   }
-  if (a.tp_slots) {
-    // Tensor-parallel reduction of the previous row-parallel matvec: wait until every rank's CTAs
-    // have delivered their partial rows into this rank's slots, then add them in rank order (the
-    // same order on every rank, so all ranks hold bit-identical x).
-    const unsigned target = a.step->epoch * (unsigned)a.tp_in_grid;
-    if (t < a.tp_size && !wait_counter_geq(a.tp_counters + t, target, a.status)) s_abort = 1;
-    named_sync(1, NT);
-    const int w_begin = (int)((long long)n_chunks * blockIdx.x / G);
-    const int w_end = (int)((long long)n_chunks * (blockIdx.x + 1) / G);
+  if (t == 0) timeline_stamp(a.trace, a.trace_stride, 1);
+  if (TPIN && a.tp_ll) {
+    // Tensor-parallel reduction of the previous row-parallel matvec: read every rank's partial
+    // rows as they arrive (each word tagged with the step epoch) and add them in rank order (the
+    // same order on every rank, so all ranks hold bit-identical x).  Per rank, the loads of all this
+    // thread's chunks are issued together, so a rank whose words are all present costs one L2
+    // round trip.
+    const unsigned ep = a.step->epoch;
+    bool ok = true;
+    constexpr int KB = KPT < 2 ? KPT : 2;  // chunks per round trip (bounds the registers held)
+    for (int r = 0; r < a.tp_size && ok; ++r) {
+      const unsigned long long* src = a.tp_ll + (size_t)r * C;
 #pragma unroll
-    for (int k = 0; k < KPT; ++k) {
-      const int c = k * NT + t;
-      if (c < n_chunks) {
-        for (int r = 0; r < a.tp_size; ++r) {
-          const float4* sp = reinterpret_cast<const float4*>(a.tp_slots + (size_t)r * C) + 2 * c;
-          const float4 p0 = __ldcg(sp), p1 = __ldcg(sp + 1);
-          xr[k][0].x += p0.x; xr[k][0].y += p0.y; xr[k][0].z += p0.z; xr[k][0].w += p0.w;
-          xr[k][1].x += p1.x; xr[k][1].y += p1.y; xr[k][1].z += p1.z; xr[k][1].w += p1.w;
+      for (int k0 = 0; k0 < KPT; k0 += KB) {
+        unsigned long long w[KB][8];
+        long long t0 = 0;
+        for (bool first = true;; first = false) {
+          bool ready = true;
+#pragma unroll
+          for (int kk = 0; kk < KB; ++kk) {
+            const int c = (k0 + kk) * NT + t;
+            if (k0 + kk < KPT && c < n_chunks) ll_load8(src + 8 * (size_t)c, w[kk]);
+          }
+#pragma unroll
+          for (int kk = 0; kk < KB; ++kk)
+            if (k0 + kk < KPT && (k0 + kk) * NT + t < n_chunks) ready = ready && ll_ready8(w[kk], ep);
+          if (ready) break;
+          if (first) {
+            t0 = clock64();
+          } else if (clock64() - t0 > kWaitBudgetCycles) {
+            atomicOr(a.status, kStatusPeerTimeout);
+            ok = false;
+            break;
+          }
+          __nanosleep(100);
         }
-        if (a.x_out && c >= w_begin && c < w_end) {
+        if (!ok) break;
+#pragma unroll
+        for (int kk = 0; kk < KB; ++kk) {
+          const int k = k0 + kk;
+          if (k < KPT && k * NT + t < n_chunks) {
+            xr[k][0].x += __uint_as_float((unsigned)w[kk][0]); xr[k][0].y += __uint_as_float((unsigned)w[kk][1]);
+            xr[k][0].z += __uint_as_float((unsigned)w[kk][2]); xr[k][0].w += __uint_as_float((unsigned)w[kk][3]);
+            xr[k][1].x += __uint_as_float((unsigned)w[kk][4]); xr[k][1].y += __uint_as_float((unsigned)w[kk][5]);
+            xr[k][1].z += __uint_as_float((unsigned)w[kk][6]); xr[k][1].w += __uint_as_float((unsigned)w[kk][7]);
+          }
+        }
+      }
+    }
+    if (!ok) s_abort = 1;
+    if (a.x_out) {
+      const int w_begin = (int)((long long)n_chunks * blockIdx.x / G);
+      const int w_end = (int)((long long)n_chunks * (blockIdx.x + 1) / G);
+#pragma unroll
+      for (int k = 0; k < KPT; ++k) {
+        const int c = k * NT + t;
+        if (c < n_chunks && c >= w_begin && c < w_end) {
           reinterpret_cast<float4*>(a.x_out)[2 * c] = xr[k][0];
           reinterpret_cast<float4*>(a.x_out)[2 * c + 1] = xr[k][1];
         }
       }
     }
+    if (t == 0) timeline_stamp(a.trace, a.trace_stride, 2);
   }
   if (NORM) {
     // RMSNorm (yalm src/infer.cpp:136-146): scale = 1 / sqrt(mean(x^2) + eps); x * scale * w
@@ -221,6 +284,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
   }
   named_sync(1, NT);
   if (s_abort) return;
+  if (t == 0) timeline_stamp(a.trace, a.trace_stride, 3);
 
   // -------------------------------------------------------------------- epilogue
   const int n_rows = min(n_st * RT, a.rows - row_begin);
@@ -234,18 +298,21 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
         a.y[row] = s;
       } else if (EPI == kEpiResid) {
         a.y[row] += s;
+      } else if (EPI == kEpiResidTP) {
+        // tensor parallel: this rank's partial for `row`, tagged with the epoch, to every rank
+        const unsigned ep = a.step->epoch;
+        for (int p = 0; p < a.tp_size; ++p) st_ll(a.peer_ll[p] + row, s, ep);
       } else {
-        // tensor parallel: this rank's value for `row` goes to every rank's buffer
+        // tensor-parallel logits: this rank's rows go to every rank's buffer
         for (int p = 0; p < a.tp_size; ++p) a.peer_slots[p][a.row_offset + row] = s;
       }
     }
-    if (EPI == kEpiResidTP || EPI == kEpiStoreTP) {
-      // Publish: all partial rows of this CTA are written before the counters move.
-      __threadfence_system();
+    if (EPI == kEpiStoreTP) {
+      // Publish: once every consumer thread has issued its peer stores, one thread per peer bumps
+      // that peer's arrival counter with a system-scope release, which orders all of the CTA's
+      // stores before the counter moves.
       named_sync(1, NT);
-      if (t < a.tp_size) {
-        atomicAdd_system(a.peer_counters[t], 1u);
-      }
+      if (t < a.tp_size) red_release_sys_add(a.peer_counters[t], 1u);
     }
   } else if (EPI == kEpiGateUp) {
     // rows (2j, 2j+1) = (w1 row j, w3 row j); yalm src/infer.cpp:367-382
@@ -322,50 +389,57 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
       }
     }
   }
+  if (t == 0) timeline_stamp(a.trace, a.trace_stride, 4);
 }
 
 // ---------------------------------------------------------------------------------- host side
 namespace {
 
-template <int KPT, int RT, int EPI, bool NORM>
+template <int KPT, int RT, int EPI, int IN>
 const void* pick4() {
-  return reinterpret_cast<const void*>(&gemv_kernel<kGemvWarps, KPT, RT, EPI, NORM>);
+  return reinterpret_cast<const void*>(&gemv_kernel<kGemvWarps, KPT, RT, EPI, IN>);
 }
 // Instantiated combinations: residual epilogues never normalise their input; the tensor-parallel
-// logits epilogue always does; pair epilogues (gate/up, QKV) need at least two rows per stage.
+// logits epilogue always does; pair epilogues (gate/up, QKV) need at least two rows per stage; the
+// tensor-parallel input (in == 2) exists for the normalised dim-wide inputs (KPT <= 4, dim <= 8192)
+// of the QKV, gate/up and logits matvecs.
 template <int KPT, int RT>
-const void* pick2(int epi, bool norm) {
+const void* pick2(int epi, int in) {
   constexpr int RP = RT >= 2 ? RT : 2;
+  constexpr bool TPK = KPT <= 4;
   switch (epi) {
-    case kEpiStore: return norm ? pick4<KPT, RT, kEpiStore, true>() : pick4<KPT, RT, kEpiStore, false>();
-    case kEpiResid: return norm ? nullptr : pick4<KPT, RT, kEpiResid, false>();
+    case kEpiStore:
+      return in == 0 ? pick4<KPT, RT, kEpiStore, 0>() : in == 1 ? pick4<KPT, RT, kEpiStore, 1>() : nullptr;
+    case kEpiResid: return in == 0 ? pick4<KPT, RT, kEpiResid, 0>() : nullptr;
     case kEpiGateUp:
       if (RT < 2) return nullptr;
-      return norm ? pick4<KPT, RP, kEpiGateUp, true>() : pick4<KPT, RP, kEpiGateUp, false>();
+      if (in == 2) return TPK ? pick4<KPT, RP, kEpiGateUp, TPK ? 2 : 1>() : nullptr;
+      return in == 1 ? pick4<KPT, RP, kEpiGateUp, 1>() : pick4<KPT, RP, kEpiGateUp, 0>();
     case kEpiQKV:
       if (RT < 2) return nullptr;
-      return norm ? pick4<KPT, RP, kEpiQKV, true>() : pick4<KPT, RP, kEpiQKV, false>();
-    case kEpiResidTP: return norm ? nullptr : pick4<KPT, RT, kEpiResidTP, false>();
-    case kEpiStoreTP: return norm ? pick4<KPT, RT, kEpiStoreTP, true>() : nullptr;
+      if (in == 2) return TPK ? pick4<KPT, RP, kEpiQKV, TPK ? 2 : 1>() : nullptr;
+      return in == 1 ? pick4<KPT, RP, kEpiQKV, 1>() : pick4<KPT, RP, kEpiQKV, 0>();
+    case kEpiResidTP: return in == 0 ? pick4<KPT, RT, kEpiResidTP, 0>() : nullptr;
+    case kEpiStoreTP: return in == 2 && TPK ? pick4<KPT, RT, kEpiStoreTP, TPK ? 2 : 1>() : nullptr;
   }
   return nullptr;
 }
 template <int KPT>
-const void* pick1(int rt, int epi, bool norm) {
+const void* pick1(int rt, int epi, int in) {
   switch (rt) {
-    case 1: return pick2<KPT, 1>(epi, norm);
-    case 2: return pick2<KPT, 2>(epi, norm);
-    case 4: return pick2<KPT, 4>(epi, norm);
-    case 8: return pick2<KPT, 8>(epi, norm);
+    case 1: return pick2<KPT, 1>(epi, in);
+    case 2: return pick2<KPT, 2>(epi, in);
+    case 4: return pick2<KPT, 4>(epi, in);
+    case 8: return pick2<KPT, 8>(epi, in);
   }
   return nullptr;
 }
-const void* pick(int kpt, int rt, int epi, bool norm) {
+const void* pick(int kpt, int rt, int epi, int in) {
   switch (kpt) {
-    case 1: return pick1<1>(rt, epi, norm);
-    case 2: return pick1<2>(rt, epi, norm);
-    case 4: return pick1<4>(rt, epi, norm);
-    case 7: return pick1<7>(rt, epi, norm);
+    case 1: return pick1<1>(rt, epi, in);
+    case 2: return pick1<2>(rt, epi, in);
+    case 4: return pick1<4>(rt, epi, in);
+    case 7: return pick1<7>(rt, epi, in);
   }
   return nullptr;
 }
@@ -414,7 +488,7 @@ int gemv_kpt_for(int cols) {
   return -1;
 }
 
-GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune) {
+GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune, bool tp_in) {
   GemvPlan p{};
   p.ok = false;
   if (cols <= 0 || rows <= 0 || (cols % 8) != 0) return p;
@@ -441,7 +515,8 @@ GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const Laun
   if (ns < 2) ns = 2;
   p.n_slots = ns;
   p.smem = (size_t)ns * p.stage_bytes + (size_t)p.red_floats * 4 + 32 * 4 + (size_t)ns * 2 * 8;
-  p.fn = pick(p.kpt, p.rt, epi, norm);
+  if (tp_in && !norm) return p;
+  p.fn = pick(p.kpt, p.rt, epi, tp_in ? 2 : norm ? 1 : 0);
   p.norm = norm;
   p.ok = p.fn != nullptr && p.smem <= 226 * 1024;
   return p;

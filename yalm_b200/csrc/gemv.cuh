@@ -54,23 +54,32 @@ struct GemvArgs {
   int pos, kv_pos, kv_sink;  // used when step == nullptr (standalone launches)
   __half* k_cache;        // [kv_heads][max_seq_len][head_dim] for this layer
   __half* v_cache;
-  // kEpiResidTP / kEpiStoreTP: per rank, the destination base in that rank's memory and the
-  // arrival counter (for this rank) that each CTA bumps once its rows are written
+  // kEpiResidTP: per rank p, where this rank's partial rows go in p's exchange region, written as
+  // 8-byte words {fp32 bits, step epoch} (no fence and no counter: the reader checks the epoch half
+  // of every word).  kEpiStoreTP: per rank p, p's fp32 logits buffer and p's arrival counter for this
+  // rank, bumped with a system-scope release once the CTA's rows are written.
+  unsigned long long* const* peer_ll;
   float* const* peer_slots;
   unsigned* const* peer_counters;
   int tp_size;
   int row_offset;
-  // tensor-parallel input: x_in = x + sum over ranks r (in rank order) of tp_slots[r * cols ..],
-  // after each rank's counter reached epoch * tp_in_grid.  x_out (if non-null) receives x_in,
-  // each CTA writing its share of the chunks.
-  const float* tp_slots;
-  const unsigned* tp_counters;
-  int tp_in_grid;
+  // tensor-parallel input: x_in = x + sum over ranks r (in rank order) of the fp32 halves of
+  // tp_ll[r * cols ..], each word read once its epoch half equals the step's epoch.  x_out (if
+  // non-null) receives x_in, each CTA writing its share of the chunks.
+  const unsigned long long* tp_ll;
   float* x_out;
   // optional L2 warm-up of another matrix (the next small matvec's weights), split across CTAs and
   // issued once after this CTA's ring fill
   const unsigned char* pf_src;
   long long pf_bytes;
+  // kEpiQKV: non-zero = also warm L2 with this layer's K/V cache slots [0, kv_len) (kv_len as the
+  // step state shows it when the producer starts), split across CTAs, for the attention kernel
+  int kv_prefetch;
+  // optional timeline (null = off): per CTA, trace[cta * trace_stride + j] = %globaltimer at
+  // j = 0 entry, 1 input vector loaded, 2 tensor-parallel inputs summed, 3 last stage consumed,
+  // 4 epilogue done
+  unsigned long long* trace;
+  int trace_stride;
 };
 
 }  // namespace yb

@@ -38,7 +38,9 @@ struct GemvPlan {
 };
 
 int gemv_kpt_for(int cols);
-GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune);
+// tp_in: the kernel also adds the tensor-parallel partial sums of the previous row-parallel matvec
+// to its (normalised) input (GemvArgs::tp_ll).
+GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune, bool tp_in = false);
 cudaError_t gemv_prepare(const GemvPlan& p);  // once per plan, outside stream capture
 cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages);
 

@@ -59,7 +59,7 @@ extern "C" int yb_attention_dev_noalloc(float* out, const float* q, const uint16
     return set_error(YB_E_INVALID, "attention scratch of " + std::to_string(need) + " bytes exceeds the " +
                                        std::to_string(kNoAllocScratchBytes) +
                                        "-byte fixed buffer of yb_attention_dev_noalloc (n_heads * "
-                                       "ceil(max_seq_len / 128) * (head_dim + 2) * 4 + n_kv_heads * 4)");
+                                       "ceil(max_seq_len / 128) * (head_dim + 4) * 4 + n_kv_heads * 4)");
   void* base = nullptr;
   int rc = scratch_address(&base);
   if (rc) return rc;

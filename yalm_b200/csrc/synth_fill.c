@@ -7,8 +7,15 @@
  * taken from one splitmix64 output per element pair.
  */
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
 #include <string.h>
+
+/* Thread count for the fills (launchers such as torchrun set OMP_NUM_THREADS=1 per process, which
+ * would make a 7B checkpoint take minutes to generate). */
+void synth_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+}
 
 static inline uint64_t splitmix64(uint64_t z) {
   z += 0x9e3779b97f4a7c15ull;

@@ -98,10 +98,10 @@ def bench_qkv(dim, nh, nkv, hd, msl, iters, seed=0):
             "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
 
 
-def bench_attention(nh, nkv, hd, kv_len, iters, seed=0):
+def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
     import torch
     g = torch.Generator(device="cuda").manual_seed(seed)
-    msl = kv_len
+    msl = kv_len if msl is None else max(msl, kv_len)
     kvbytes = 2 * nkv * msl * hd * 2
     n = _copies(kvbytes)
     ks = [torch.randn(nkv, msl, hd, device="cuda", generator=g).half() for _ in range(n)]
@@ -116,7 +116,7 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0):
                   _p(scratch), stream)
     ms = _time(fn, iters)
     nbytes = kvbytes + 2 * nh * hd * 4
-    return {"kernel": "attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "kv_len": kv_len,
+    return {"kernel": "attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "kv_len": kv_len, "max_seq_len": msl,
             "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
 
 
@@ -125,6 +125,8 @@ def main(argv=None):
     ap.add_argument("--kernel", default="all", choices=["gemv", "gateup", "qkv", "attention", "all"])
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--quick", action="store_true", help="one shape per kernel (for profiler captures)")
+    ap.add_argument("--kv-lens", default="", help="attention: comma-separated kv_len values")
+    ap.add_argument("--msl", type=int, default=0, help="attention: cache capacity (default: kv_len)")
     args = ap.parse_args(argv)
     import torch
     torch.cuda.set_device(0)
@@ -139,8 +141,10 @@ def main(argv=None):
         rows.append(bench_qkv(4096, 32, 8, 128, 4096, args.iters))
     if args.kernel in ("attention", "all"):
         lens = [4096] if args.quick else [128, 1024, 4096, 16384, 32768]
+        if args.kv_lens:
+            lens = [int(v) for v in args.kv_lens.split(",")]
         for kv in lens:
-            rows.append(bench_attention(32, 8, 128, kv, args.iters))
+            rows.append(bench_attention(32, 8, 128, kv, args.iters, msl=args.msl or None))
     for r in rows:
         print(json.dumps(r))
 

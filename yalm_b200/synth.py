@@ -130,6 +130,8 @@ def _synth_lib():
         _lib.synth_fill_normal_f16.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint64,
                                                ctypes.c_uint64, ctypes.c_float]
         _lib.synth_fill_const_f32.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_float]
+        _lib.synth_set_threads.argtypes = [ctypes.c_int]
+        _lib.synth_set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
     return _lib
 
 
