@@ -11,9 +11,11 @@ KV length distribution stays that of the config.  One step = one decode token = 
 
   value  tok/s with everything resident on the device: K back-to-back yb_forward_async steps
          (teacher-forced tokens), CUDA events on the engine stream, max over ranks.
-  e2e    the same metric through the public C-ABI call a yalm caller makes (yb_forward with a host
-         logits buffer: token id in, 128 KB of fp32 logits out to pinned host memory, greedy argmax
-         on the host picks the next token), wall clock around the K calls.
+  e2e    the same metric through the public C-ABI call a yalm decode loop makes, wall clock around
+         the K calls: yb_forward_sample (Model::forward + Sampler::sample at temperature 0 with the
+         sampler on the device: token id in, next id out).  e2e.logits_to_host is the same loop
+         through yb_forward with 128 KB of fp32 logits copied to pinned host memory and the argmax
+         taken on the host.
 Under torchrun (N > 1) each rank is one tensor-parallel shard (heads, kv heads, FFN hidden and
 vocabulary split N ways); partial sums cross NVLink inside the wo / w2 kernels.
 """
@@ -200,6 +202,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     path = model_file(args.config, rank, world, dist)
@@ -253,6 +256,29 @@ def main():
     value = args.steps / (ms_dev / 1000.0)
 
     # ---------------------------------------------------------------- end to end through the C ABI
+    # (a) yb_forward_sample: the decode loop of yalm's main.cpp (forward + Sampler::sample at
+    # temperature 0) with the sampler on the device: token id in, next token id (4 bytes) out.
+    e2e_steps = args.steps
+    tok = int(prompt[-1])
+    for pos, t_ in enumerate(prompt[:-1]):
+        m.forward_async(int(t_), pos, InferenceMode.HYDRATE_KV_CACHE)
+    tok = m.forward_sample(tok, PROMPT_LEN - 1)
+    for i in range(args.warmup):
+        tok = m.forward_sample(tok, pos_of(i))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        tok = m.forward_sample(tok, pos_of(args.warmup + i))
+    t_e2e = time.perf_counter() - t0
+    if world > 1:
+        tt = torch.tensor([t_e2e], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_e2e = float(tt.item())
+    e2e = e2e_steps / t_e2e
+
+    # (b) yb_forward with the full logits copied to pinned host memory and greedy argmax on the host
     logits_host = torch.empty(c.vocab_size, dtype=torch.float32, pin_memory=True)
     lg = logits_host.numpy()
 
@@ -261,9 +287,8 @@ def main():
             return lg
 
     ps = PinnedState(c)
-    for pos, tok in enumerate(prompt):
-        m.forward(ps, int(tok), pos, InferenceMode.OUTPUT_LOGITS if pos + 1 == PROMPT_LEN else InferenceMode.HYDRATE_KV_CACHE)
-    e2e_steps = args.steps
+    for pos, t_ in enumerate(prompt):
+        m.forward(ps, int(t_), pos, InferenceMode.OUTPUT_LOGITS if pos + 1 == PROMPT_LEN else InferenceMode.HYDRATE_KV_CACHE)
     for i in range(args.warmup):
         m.forward(ps, int(np.argmax(lg)), pos_of(i))
     if world > 1:
@@ -271,14 +296,13 @@ def main():
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
-        tok = int(np.argmax(lg))  # greedy, as yalm's sampler at temperature 0 (sampler.cpp:27-38)
-        m.forward(ps, tok, pos_of(args.warmup + i))
-    t_e2e = time.perf_counter() - t0
+        m.forward(ps, int(np.argmax(lg)), pos_of(args.warmup + i))  # greedy, sampler.cpp:27-38
+    t_l = time.perf_counter() - t0
     if world > 1:
-        tt = torch.tensor([t_e2e], device="cuda")
+        tt = torch.tensor([t_l], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_e2e = float(tt.item())
-    e2e = e2e_steps / t_e2e
+        t_l = float(tt.item())
+    e2e_logits = e2e_steps / t_l
 
     # ---------------------------------------------------------------- dominant kernel roofline
     peak, peak_kind = measured_peaks()
@@ -353,6 +377,7 @@ def main():
             launches_per_step = 1
         else:
             launches_per_step = 1 + c.n_layers * (4 + m_w2_panels(m)) + 1 + (1 if world > 1 else 0)
+        # the timed `value` region runs K logits-mode steps (no sampler kernel)
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_dev / args.steps, 4), "higher_is_better": True,
@@ -363,8 +388,10 @@ def main():
                        "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_LEN, "context": c.max_seq_len,
                        "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights streamed every step: "
                                                           f"{step_bytes / 1e9:.2f} GB/step/rank)"},
-            "e2e": {"value": round(e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 4 * c.vocab_size},
+            "e2e": {"value": round(e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+                    "api": "yb_forward_sample (greedy on the device)",
+                    "logits_to_host": {"value": round(e2e_logits, 3), "api": "yb_forward + host argmax",
+                                       "d2h_bytes_per_step": 4 * c.vocab_size}},
             "roofline": roofline,
             "step_roofline": {"bytes_per_step_per_rank": step_bytes, "achieved_gbs": round(step_gbs, 1), "peak": peak,
                               "frac": round(step_gbs / peak, 4)},

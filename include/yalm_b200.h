@@ -94,6 +94,20 @@ int yb_create(const yb_config* cfg, const yb_weights* w, int device, int tp_rank
  * cache is updated; returns without waiting for the GPU, `logits` is ignored. */
 int yb_forward(yb_engine* e, int token, int pos, int mode, float* logits);
 
+/* One decode step in logits mode followed by yalm's sampler on the device, replacing
+ * Model::forward + Sampler::sample (src/sampler.cpp:27-64): only the chosen id comes back to the
+ * host (4 bytes instead of vocab_size fp32 logits).  temperature 0: greedy, the first index of the
+ * maximum logit (sample_argmax, src/sampler.cpp:27-38).  temperature > 0: the first index whose
+ * running sum of softmax(logits / temperature) reaches `coin` (yalm draws coin = rand() / RAND_MAX on
+ * the host, src/sampler.cpp:55; pass the same value), else vocab_size - 1; the running sum is
+ * formed in parallel, so the id can differ from yalm's sequential scan only when coin lies within
+ * float rounding of a boundary.  Returns after the step; the logits stay on the device. */
+int yb_forward_sample(yb_engine* e, int token, int pos, float temperature, float coin, int* next_token);
+
+/* One decode step in logits mode followed by Sampler::sample_prob(target) on the device
+ * (src/sampler.cpp:11-25, perplexity mode): *prob = exp(l_target - max) / sum_i exp(l_i - max). */
+int yb_forward_prob(yb_engine* e, int token, int pos, int target, float* prob);
+
 /* Same step, logits left on the device (yb_logits_dev) and no host synchronisation: for
  * device-resident pipelines and benchmarks.  Follow with yb_sync before reading results. */
 int yb_forward_async(yb_engine* e, int token, int pos, int mode);

@@ -53,6 +53,8 @@ _I, _F, _S = ctypes.c_int, ctypes.c_float, ctypes.c_size_t
 _SIGS = {
     "yb_create": (_I, [ctypes.POINTER(yb_config), ctypes.POINTER(yb_weights), _I, _I, _I, ctypes.POINTER(_P)]),
     "yb_forward": (_I, [_P, _I, _I, _I, _P]),
+    "yb_forward_sample": (_I, [_P, _I, _I, ctypes.c_float, ctypes.c_float, _P]),
+    "yb_forward_prob": (_I, [_P, _I, _I, _I, _P]),
     "yb_forward_async": (_I, [_P, _I, _I, _I]),
     "yb_sync": (_I, [_P]),
     "yb_logits_dev": (_P, [_P]),

@@ -245,6 +245,12 @@ struct StepState {
   unsigned epoch;   // forward-call counter, identical on every tensor-parallel rank
   unsigned lepoch;  // counter of forward calls that produced logits
   int pad;
+  // on-device sampler (yb_forward_sample / yb_forward_prob): op 0 argmax, 1 temperature sample,
+  // 2 probability of `target`
+  int sample_op;
+  int sample_target;
+  float temperature;
+  float coin;
 };
 
 }  // namespace yb

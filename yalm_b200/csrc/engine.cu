@@ -41,6 +41,10 @@ __global__ void step_kernel(const StepArgs a) {
     s.epoch = a.epoch;
     s.lepoch = a.lepoch;
     s.pad = 0;
+    s.sample_op = a.sample_op;
+    s.sample_target = a.sample_target;
+    s.temperature = a.temperature;
+    s.coin = a.coin;
     *a.step = s;
   }
   // embedding row -> fp32 residual stream (src/infer.cpp:460-481)
@@ -167,6 +171,21 @@ static GemvArgs base_args(yb_engine* e) {
   a.eps = e->cfg.norm_eps;
   a.tp_size = e->tp_size;
   return a;
+}
+
+// The sampler after the classifier: one CTA over the logits every rank holds.
+static int launch_sampler(yb_engine* e, cudaStream_t s, const StepState* step, SampleParams direct) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kSampleThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  YB_CK(cudaLaunchKernelEx(&cfg, sample_kernel, yb_logits_dev(e), e->cfg.vocab_size, step, direct, e->sample_d));
+  return 0;
 }
 
 int record_step(yb_engine* e, int mode, const StepArgs& sa) {
@@ -298,7 +317,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       }
     }
   }
-  if (mode == YB_MODE_OUTPUT_LOGITS) {
+  if (mode != kStepHydrate) {
     GemvArgs a = base_args(e);
     a.w = e->wcls;
     a.ldw = c.dim;
@@ -336,12 +355,16 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       cfg.numAttrs = 1;
       YB_CK(cudaLaunchKernelEx(&cfg, tp_gather_wait_kernel, wa.step, wa.counters, wa.tp_size, wa.grid, wa.status));
     }
+    if (mode == kStepSample) {
+      const int rc = launch_sampler(e, s, e->step, SampleParams{});
+      if (rc) return rc;
+    }
   }
   return 0;
 }
 
 static int build_graph(yb_engine* e, int mode) {
-  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, 0, 0, e->cfg.max_seq_len, 0, 0};
+  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, 0, 0, e->cfg.max_seq_len, 0, 0, 0, 0, 0.f, 0.f};
   cudaGraph_t g = nullptr;
   YB_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
   int rc = record_step(e, mode, sa);
@@ -394,6 +417,9 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
   YB_CK(cudaHostAlloc(reinterpret_cast<void**>(&e->status_h), 64, cudaHostAllocMapped));
   std::memset(e->status_h, 0, 64);
   YB_CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->status_d), e->status_h, 0));
+  YB_CK(cudaHostAlloc(reinterpret_cast<void**>(&e->sample_h), sizeof(SampleResult), cudaHostAllocMapped));
+  std::memset(e->sample_h, 0, sizeof(SampleResult));
+  YB_CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->sample_d), e->sample_h, 0));
 
   if ((rc = upload_weights(e, w))) return rc;
 
@@ -524,8 +550,8 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
     return 0;
   }
   if (!e->persistent) {
-    if ((rc = build_graph(e, 0))) return rc;
-    if ((rc = build_graph(e, 1))) return rc;
+    for (int m = 0; m < kStepVariants; ++m)
+      if ((rc = build_graph(e, m))) return rc;
   }
   YB_CK(cudaDeviceSynchronize());
   return 0;
@@ -546,16 +572,17 @@ extern "C" int yb_create(const yb_config* cfg, const yb_weights* w, int device, 
   return 0;
 }
 
-static int launch_step(yb_engine* e, int token, int pos, int mode) {
+static int launch_step(yb_engine* e, int token, int pos, int mode, const SampleParams* sp = nullptr) {
   if (!e) return set_error(YB_E_INVALID, "null engine");
-  if (mode != 0 && mode != 1) return set_error(YB_E_INVALID, "mode must be 0 (hydrate) or 1 (logits)");
+  if (mode != kStepHydrate && mode != kStepLogits && !(mode == kStepSample && sp))
+    return set_error(YB_E_INVALID, "mode must be 0 (hydrate) or 1 (logits)");
   if (token < 0 || token >= e->cfg.vocab_size) return set_error(YB_E_INVALID, "token out of range");
   if (pos < 0) return set_error(YB_E_INVALID, "negative position");
   if (!e->persistent && !e->exec[mode])
     return set_error(YB_E_INVALID, "engine not ready (tensor-parallel engines need yb_tp_import)");
   YB_CK(cudaSetDevice(e->device));
   e->epoch += 1;
-  if (mode == YB_MODE_OUTPUT_LOGITS) e->lepoch += 1;
+  if (mode != kStepHydrate) e->lepoch += 1;
   if (e->persistent) {
     const yb_config& c = e->cfg;
     PArgs a;
@@ -595,7 +622,7 @@ static int launch_step(yb_engine* e, int token, int pos, int mode) {
     a.kv_sink = pos >= c.max_seq_len ? 2 : 0;
     a.kv_pos = a.kv_sink + (pos - a.kv_sink) % (c.max_seq_len - a.kv_sink);
     a.kv_len = pos >= c.max_seq_len ? c.max_seq_len : pos + 1;
-    a.mode = mode;
+    a.mode = mode == kStepHydrate ? 0 : 1;
     a.epoch = e->epoch;
     a.lepoch = e->lepoch;
     a.tp_size = 1;
@@ -606,9 +633,15 @@ static int launch_step(yb_engine* e, int token, int pos, int mode) {
     a.trace = e->trace;
     YB_CK(cudaMemsetAsync(e->persist_sync, 0, e->persist_sync_bytes, e->stream));
     YB_CK(persist_launch(e->plan_persist, a, e->stream));
+    if (mode == kStepSample) {
+      SampleParams d = *sp;
+      d.epoch = e->epoch;
+      return launch_sampler(e, e->stream, nullptr, d);
+    }
     return 0;
   }
-  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, token, pos, e->cfg.max_seq_len, e->epoch, e->lepoch};
+  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, token, pos, e->cfg.max_seq_len, e->epoch, e->lepoch,
+              sp ? sp->op : 0, sp ? sp->target : 0, sp ? sp->temperature : 0.f, sp ? sp->coin : 0.f};
   cudaKernelNodeParams kp = {};
   void* params[] = {&sa};
   kp.func = reinterpret_cast<void*>(&step_kernel);
@@ -645,6 +678,41 @@ extern "C" int yb_forward(yb_engine* e, int token, int pos, int mode, float* log
 }
 
 extern "C" int yb_forward_async(yb_engine* e, int token, int pos, int mode) { return launch_step(e, token, pos, mode); }
+
+static int forward_sampled(yb_engine* e, int token, int pos, const SampleParams& sp, SampleResult* res) {
+  int rc = launch_step(e, token, pos, kStepSample, &sp);
+  if (rc) return rc;
+  YB_CK(cudaStreamSynchronize(e->stream));
+  if ((rc = check_status(e))) return rc;
+  const volatile SampleResult* v = e->sample_h;
+  res->token = v->token;
+  res->prob = v->prob;
+  res->epoch = v->epoch;
+  if (res->epoch != e->epoch) return set_error(YB_E_CUDA, "sampler result missing");
+  return 0;
+}
+
+extern "C" int yb_forward_sample(yb_engine* e, int token, int pos, float temperature, float coin, int* next_token) {
+  if (!next_token) return set_error(YB_E_INVALID, "null output pointer");
+  if (!(temperature >= 0.f)) return set_error(YB_E_INVALID, "temperature must be >= 0");
+  SampleParams sp{temperature == 0.f ? 0 : 1, 0, temperature, coin, 0};
+  SampleResult r;
+  int rc = forward_sampled(e, token, pos, sp, &r);
+  if (rc) return rc;
+  *next_token = r.token;
+  return 0;
+}
+
+extern "C" int yb_forward_prob(yb_engine* e, int token, int pos, int target, float* prob) {
+  if (!prob) return set_error(YB_E_INVALID, "null output pointer");
+  if (!e || target < 0 || target >= e->cfg.vocab_size) return set_error(YB_E_INVALID, "target out of range");
+  SampleParams sp{2, target, 1.f, 0.f, 0};
+  SampleResult r;
+  int rc = forward_sampled(e, token, pos, sp, &r);
+  if (rc) return rc;
+  *prob = r.prob;
+  return 0;
+}
 
 extern "C" int yb_sync(yb_engine* e) {
   if (!e) return set_error(YB_E_INVALID, "null engine");
@@ -712,7 +780,7 @@ extern "C" void yb_destroy(yb_engine* e) {
   if (!e) return;
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
-  for (int m = 0; m < 2; ++m) {
+  for (int m = 0; m < kStepVariants; ++m) {
     if (e->exec[m]) cudaGraphExecDestroy(e->exec[m]);
     if (e->graph[m]) cudaGraphDestroy(e->graph[m]);
   }
@@ -724,6 +792,7 @@ extern "C" void yb_destroy(yb_engine* e) {
   if (e->tp.base) cudaFree(e->tp.base);
   for (void* p : e->allocs) cudaFree(p);
   if (e->status_h) cudaFreeHost(e->status_h);
+  if (e->sample_h) cudaFreeHost(e->sample_h);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -884,8 +953,8 @@ extern "C" int yb_tp_import(yb_engine* e, const void* blobs, size_t stride) {
   YB_CK(cudaMemcpy(e->tp.d_peer_counters, cnts.data(), cnts.size() * sizeof(unsigned*), cudaMemcpyHostToDevice));
   e->tp.joined = true;
   int rc;
-  if ((rc = build_graph(e, 0))) return rc;
-  if ((rc = build_graph(e, 1))) return rc;
+  for (int m = 0; m < kStepVariants; ++m)
+    if ((rc = build_graph(e, m))) return rc;
   YB_CK(cudaDeviceSynchronize());
   return 0;
 }

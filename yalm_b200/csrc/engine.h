@@ -8,6 +8,7 @@
 
 #include "../../include/yalm_b200.h"
 #include "attention.cuh"
+#include "sampler.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "launch.h"
@@ -62,7 +63,14 @@ struct StepArgs {
   int max_seq_len;
   unsigned epoch;
   unsigned lepoch;
+  int sample_op;
+  int sample_target;
+  float temperature;
+  float coin;
 };
+
+// Graph / launch variants of a step: the two InferenceModes, and logits followed by the sampler.
+constexpr int kStepHydrate = 0, kStepLogits = 1, kStepSample = 2, kStepVariants = 3;
 
 }  // namespace yb
 
@@ -112,9 +120,11 @@ struct yb_engine {
   // attention, wo, gate/up, w2 panels; then the classifier) 8 stamps per CTA, [cta][kernel * 8 + j]
   unsigned long long* gtrace = nullptr;
   int gtrace_rows = 0, gtrace_events = 0;
-  cudaGraph_t graph[2] = {nullptr, nullptr};
-  cudaGraphExec_t exec[2] = {nullptr, nullptr};
-  cudaGraphNode_t step_node[2] = {nullptr, nullptr};
+  cudaGraph_t graph[yb::kStepVariants] = {};
+  cudaGraphExec_t exec[yb::kStepVariants] = {};
+  cudaGraphNode_t step_node[yb::kStepVariants] = {};
+  yb::SampleResult* sample_h = nullptr;  // host-mapped result of the on-device sampler
+  yb::SampleResult* sample_d = nullptr;
   unsigned epoch = 0;
   unsigned lepoch = 0;
   yb::TpRegion tp;

@@ -221,6 +221,21 @@ class Model:
     def forward_async(self, token: int, pos: int, mode: InferenceMode = InferenceMode.OUTPUT_LOGITS) -> None:
         _lib.call("yb_forward_async", self.engine, int(token), int(pos), int(mode))
 
+    def forward_sample(self, token: int, pos: int, temperature: float = 0.0, coin: float = 0.0) -> int:
+        """Model::forward + Sampler::sample (src/sampler.cpp:27-64) with the sampler on the device:
+        returns the next token id; temperature 0 is greedy, else `coin` plays yalm's
+        rand() / RAND_MAX draw."""
+        out = ctypes.c_int()
+        _lib.call("yb_forward_sample", self.engine, int(token), int(pos), float(temperature), float(coin),
+                  ctypes.byref(out))
+        return out.value
+
+    def forward_prob(self, token: int, pos: int, target: int) -> float:
+        """Model::forward + Sampler::sample_prob(target) (src/sampler.cpp:11-25) on the device."""
+        out = ctypes.c_float()
+        _lib.call("yb_forward_prob", self.engine, int(token), int(pos), int(target), ctypes.byref(out))
+        return out.value
+
     def sync(self) -> None:
         _lib.call("yb_sync", self.engine)
 
