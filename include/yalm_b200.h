@@ -136,7 +136,8 @@ int yb_executor(yb_engine* e);
  *    consumer end, producer end.
  *  - graph executor: 8 stamps per kernel of the step in launch order (per layer qkv, attention, wo,
  *    gate/up, w2; then the classifier in logits mode): for the matvecs j = 0 entry, 1 input vector
- *    loaded, 2 tensor-parallel partial sums added, 3 last weight stage consumed, 4 epilogue done;
+ *    loaded, 2 tensor-parallel all-reduce done (before 1), 3 last weight stage consumed, 4 epilogue
+ *    done;
  *    for attention (row = blockIdx.y * gridDim.x + blockIdx.x) 0 entry, 1 inputs ready, 2 first
  *    K/V sub-chunk staged, 5 scores done, 6 V pass done, 3 slice done, 4 exit.  Rows beyond a
  *    kernel's grid stay 0. */

@@ -47,6 +47,7 @@ __global__ void step_kernel(const StepArgs a) {
     s.coin = a.coin;
     *a.step = s;
   }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n_bar; i += gridDim.x * blockDim.x) a.bar[i] = 0u;
   // embedding row -> fp32 residual stream (src/infer.cpp:460-481)
   const __half* row = a.emb + (size_t)a.token * a.dim;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.dim; i += gridDim.x * blockDim.x)
@@ -229,6 +230,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       if (tp && l > 0) {
         // add the previous layer's w2 partials (exchange point 2l-1)
         a.tp_ll = tp_in(e, 2 * l - 1);
+        a.tp_bar = e->tp.d_bar + (2 * l - 1);
         float* x_next = (x_cur == e->x) ? e->x2 : e->x;
         a.x_out = x_next;
         x_cur = x_next;
@@ -285,6 +287,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       a.act_silu = c.act;
       if (tp) {
         a.tp_ll = tp_in(e, 2 * l);
+        a.tp_bar = e->tp.d_bar + 2 * l;
         float* x_next = (x_cur == e->x) ? e->x2 : e->x;
         a.x_out = x_next;
         x_cur = x_next;
@@ -327,6 +330,8 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
     a.norm_w = e->rms_final;
     if (tp) {
       a.tp_ll = tp_in(e, 2 * c.n_layers - 1);
+      a.tp_bar = e->tp.d_bar + (2 * c.n_layers - 1);
+      a.x_out = (x_cur == e->x) ? e->x2 : e->x;  // the final x, formed share by share
       a.peer_slots = e->tp.d_peer_slots;
       a.peer_counters = e->tp.d_peer_counters;
       a.row_offset = e->tp_rank * e->vocab_l;
@@ -364,7 +369,8 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
 }
 
 static int build_graph(yb_engine* e, int mode) {
-  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, 0, 0, e->cfg.max_seq_len, 0, 0, 0, 0, 0.f, 0.f};
+  StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, 0, 0, e->cfg.max_seq_len, 0, 0, 0, 0, 0.f, 0.f,
+              e->tp.d_bar, e->tp.d_bar ? 2 * e->cfg.n_layers : 0};
   cudaGraph_t g = nullptr;
   YB_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
   int rc = record_step(e, mode, sa);
@@ -641,7 +647,8 @@ static int launch_step(yb_engine* e, int token, int pos, int mode, const SampleP
     return 0;
   }
   StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, token, pos, e->cfg.max_seq_len, e->epoch, e->lepoch,
-              sp ? sp->op : 0, sp ? sp->target : 0, sp ? sp->temperature : 0.f, sp ? sp->coin : 0.f};
+              sp ? sp->op : 0, sp ? sp->target : 0, sp ? sp->temperature : 0.f, sp ? sp->coin : 0.f,
+              e->tp.d_bar, e->tp.d_bar ? 2 * e->cfg.n_layers : 0};
   cudaKernelNodeParams kp = {};
   void* params[] = {&sa};
   kp.func = reinterpret_cast<void*>(&step_kernel);
@@ -787,6 +794,7 @@ extern "C" void yb_destroy(yb_engine* e) {
   for (size_t i = 0; i < e->tp.peer_base.size(); ++i)
     if ((int)i != e->tp_rank && e->tp.peer_base[i]) cudaIpcCloseMemHandle(e->tp.peer_base[i]);
   if (e->tp.d_peer_ll) cudaFree(e->tp.d_peer_ll);
+  if (e->tp.d_bar) cudaFree(e->tp.d_bar);
   if (e->tp.d_peer_slots) cudaFree(e->tp.d_peer_slots);
   if (e->tp.d_peer_counters) cudaFree(e->tp.d_peer_counters);
   if (e->tp.base) cudaFree(e->tp.base);
@@ -946,6 +954,8 @@ extern "C" int yb_tp_import(yb_engine* e, const void* blobs, size_t stride) {
     cnts[p] = reinterpret_cast<unsigned*>(base + e->tp.cnt_off) + e->tp_rank;
   }
   YB_CK(cudaMalloc(&e->tp.d_peer_ll, ll.size() * sizeof(unsigned long long*)));
+  YB_CK(cudaMalloc(&e->tp.d_bar, (size_t)n_pts * sizeof(unsigned)));
+  YB_CK(cudaMemset(e->tp.d_bar, 0, (size_t)n_pts * sizeof(unsigned)));
   YB_CK(cudaMalloc(&e->tp.d_peer_slots, lg.size() * sizeof(float*)));
   YB_CK(cudaMalloc(&e->tp.d_peer_counters, cnts.size() * sizeof(unsigned*)));
   YB_CK(cudaMemcpy(e->tp.d_peer_ll, ll.data(), ll.size() * sizeof(unsigned long long*), cudaMemcpyHostToDevice));

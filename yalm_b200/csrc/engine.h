@@ -48,6 +48,7 @@ struct TpRegion {
   // device arrays of pointers used by kernels: [2*n_layers][tp] exchange destinations, [tp]
   // logits destinations and counters
   unsigned long long** d_peer_ll = nullptr;
+  unsigned* d_bar = nullptr;  // [2*n_layers] arrival counters of the in-kernel barrier, zeroed per step
   float** d_peer_slots = nullptr;
   unsigned** d_peer_counters = nullptr;
   bool joined = false;
@@ -67,6 +68,8 @@ struct StepArgs {
   int sample_target;
   float temperature;
   float coin;
+  unsigned* bar;  // counters the step kernel zeroes (tensor-parallel barriers), n_bar of them
+  int n_bar;
 };
 
 // Graph / launch variants of a step: the two InferenceModes, and logits followed by the sampler.

@@ -141,43 +141,34 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
 
   pdl_wait();  // activations below are produced by the previous kernel of the step
 
-#pragma unroll
-  for (int k = 0; k < KPT; ++k) {
-    const int c = k * NT + t;
-    if (c < n_chunks) {
-      xr[k][0] = reinterpret_cast<const float4*>(a.x)[2 * c];
-      xr[k][1] = reinterpret_cast<const float4*>(a.x)[2 * c + 1];
-    } else {
-      xr[k][0] = make_float4(0.f, 0.f, 0.f, 0.f);
-      xr[k][1] = xr[k][0];
-    }
-  }
-  if (t == 0) timeline_stamp(a.trace, a.trace_stride, 1);
+  const float* xin = a.x;
   if (TPIN && a.tp_ll) {
-    // Tensor-parallel reduction of the previous row-parallel matvec: read every rank's partial
-    // rows as they arrive (each word tagged with the step epoch) and add them in rank order (the
-    // same order on every rank, so all ranks hold bit-identical x).  Per rank, the loads of all this
-    // thread's chunks are issued together, so a rank whose words are all present costs one L2
-    // round trip.
+    // Tensor-parallel all-reduce of the previous row-parallel matvec, in two parts.
+    // (1) This CTA's share of x (chunks [w_begin, w_end)): the residual plus every rank's partial,
+    //     added in rank order (the same order on every rank, so all ranks hold bit-identical x),
+    //     each partial read once its exchange word carries this step's epoch; written to x_out.
+    // (2) A barrier over this kernel's CTAs (all resident: the grid is at most one CTA per slot),
+    //     after which every CTA reads the whole new x from x_out.  Each CTA so reads P words per
+    //     element of its share instead of P words per element of x.
     const unsigned ep = a.step->epoch;
+    const int w_begin = (int)((long long)n_chunks * blockIdx.x / G);
+    const int w_end = (int)((long long)n_chunks * (blockIdx.x + 1) / G);
     bool ok = true;
-    constexpr int KB = KPT < 2 ? KPT : 2;  // chunks per round trip (bounds the registers held)
-    for (int r = 0; r < a.tp_size && ok; ++r) {
-      const unsigned long long* src = a.tp_ll + (size_t)r * C;
-#pragma unroll
-      for (int k0 = 0; k0 < KPT; k0 += KB) {
-        unsigned long long w[KB][8];
+    for (int e = w_begin * 8 + t; e < w_end * 8; e += NT) {
+      float v = a.x[e];
+      for (int r0 = 0; r0 < a.tp_size && ok; r0 += 8) {
+        const int nr = min(8, a.tp_size - r0);
+        unsigned long long w[8];
         long long t0 = 0;
         for (bool first = true;; first = false) {
           bool ready = true;
 #pragma unroll
-          for (int kk = 0; kk < KB; ++kk) {
-            const int c = (k0 + kk) * NT + t;
-            if (k0 + kk < KPT && c < n_chunks) ll_load8(src + 8 * (size_t)c, w[kk]);
-          }
+          for (int j = 0; j < 8; ++j)
+            if (j < nr)
+              asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w[j]) : "l"(a.tp_ll + (size_t)(r0 + j) * C + e) : "memory");
 #pragma unroll
-          for (int kk = 0; kk < KB; ++kk)
-            if (k0 + kk < KPT && (k0 + kk) * NT + t < n_chunks) ready = ready && ll_ready8(w[kk], ep);
+          for (int j = 0; j < 8; ++j)
+            if (j < nr) ready = ready && (unsigned)(w[j] >> 32) == ep;
           if (ready) break;
           if (first) {
             t0 = clock64();
@@ -188,34 +179,53 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
           }
           __nanosleep(100);
         }
-        if (!ok) break;
+        if (ok) {
 #pragma unroll
-        for (int kk = 0; kk < KB; ++kk) {
-          const int k = k0 + kk;
-          if (k < KPT && k * NT + t < n_chunks) {
-            xr[k][0].x += __uint_as_float((unsigned)w[kk][0]); xr[k][0].y += __uint_as_float((unsigned)w[kk][1]);
-            xr[k][0].z += __uint_as_float((unsigned)w[kk][2]); xr[k][0].w += __uint_as_float((unsigned)w[kk][3]);
-            xr[k][1].x += __uint_as_float((unsigned)w[kk][4]); xr[k][1].y += __uint_as_float((unsigned)w[kk][5]);
-            xr[k][1].z += __uint_as_float((unsigned)w[kk][6]); xr[k][1].w += __uint_as_float((unsigned)w[kk][7]);
-          }
+          for (int j = 0; j < 8; ++j)
+            if (j < nr) v += __uint_as_float((unsigned)w[j]);
         }
       }
+      a.x_out[e] = v;
     }
     if (!ok) s_abort = 1;
-    if (a.x_out) {
-      const int w_begin = (int)((long long)n_chunks * blockIdx.x / G);
-      const int w_end = (int)((long long)n_chunks * (blockIdx.x + 1) / G);
-#pragma unroll
-      for (int k = 0; k < KPT; ++k) {
-        const int c = k * NT + t;
-        if (c < n_chunks && c >= w_begin && c < w_end) {
-          reinterpret_cast<float4*>(a.x_out)[2 * c] = xr[k][0];
-          reinterpret_cast<float4*>(a.x_out)[2 * c + 1] = xr[k][1];
+    named_sync(1, NT);
+    if (t == 0) {
+      // release this CTA's share, then wait (bounded) for every CTA's
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.tp_bar) : "memory");
+      long long t0 = clock64();
+      unsigned seen;
+      do {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(a.tp_bar) : "memory");
+        if ((int)(seen - (unsigned)G) >= 0) break;
+        if (clock64() - t0 > kWaitBudgetCycles) {
+          atomicOr(a.status, kStatusPeerTimeout);
+          s_abort = 1;
+          break;
         }
-      }
+        __nanosleep(64);
+      } while (true);
     }
+    named_sync(1, NT);
+    xin = a.x_out;
     if (t == 0) timeline_stamp(a.trace, a.trace_stride, 2);
   }
+#pragma unroll
+  for (int k = 0; k < KPT; ++k) {
+    const int c = k * NT + t;
+    if (c < n_chunks) {
+      if (TPIN && a.tp_ll) {  // written by other CTAs of this kernel: read through L2
+        xr[k][0] = __ldcg(reinterpret_cast<const float4*>(xin) + 2 * c);
+        xr[k][1] = __ldcg(reinterpret_cast<const float4*>(xin) + 2 * c + 1);
+      } else {
+        xr[k][0] = reinterpret_cast<const float4*>(xin)[2 * c];
+        xr[k][1] = reinterpret_cast<const float4*>(xin)[2 * c + 1];
+      }
+    } else {
+      xr[k][0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      xr[k][1] = xr[k][0];
+    }
+  }
+  if (t == 0) timeline_stamp(a.trace, a.trace_stride, 1);
   if (NORM) {
     // RMSNorm (yalm src/infer.cpp:136-146): scale = 1 / sqrt(mean(x^2) + eps); x * scale * w
     float ss = 0.f;

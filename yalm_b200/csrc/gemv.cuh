@@ -64,10 +64,12 @@ struct GemvArgs {
   int tp_size;
   int row_offset;
   // tensor-parallel input: x_in = x + sum over ranks r (in rank order) of the fp32 halves of
-  // tp_ll[r * cols ..], each word read once its epoch half equals the step's epoch.  x_out (if
-  // non-null) receives x_in, each CTA writing its share of the chunks.
+  // tp_ll[r * cols ..], each word read once its epoch half equals the step's epoch.  Each CTA forms
+  // its share of x_in into x_out (required), bumps tp_bar (zeroed by the step kernel) and, once all
+  // gridDim.x CTAs have, reads x_in back from x_out.
   const unsigned long long* tp_ll;
   float* x_out;
+  unsigned* tp_bar;
   // optional L2 warm-up of another matrix (the next small matvec's weights), split across CTAs and
   // issued once after this CTA's ring fill
   const unsigned char* pf_src;
@@ -76,8 +78,8 @@ struct GemvArgs {
   // step state shows it when the producer starts), split across CTAs, for the attention kernel
   int kv_prefetch;
   // optional timeline (null = off): per CTA, trace[cta * trace_stride + j] = %globaltimer at
-  // j = 0 entry, 1 input vector loaded, 2 tensor-parallel inputs summed, 3 last stage consumed,
-  // 4 epilogue done
+  // j = 0 entry, 1 input vector loaded, 2 tensor-parallel all-reduce done (before 1), 3 last stage
+  // consumed, 4 epilogue done
   unsigned long long* trace;
   int trace_stride;
 };
