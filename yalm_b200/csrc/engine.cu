@@ -11,6 +11,7 @@
 // the wo/w2 matvecs push their partial rows into every rank's exchange slots over NVLink peer
 // memory and the following matvec adds them up (no separate collective kernel).
 #include "engine.h"
+#include "loader.h"
 
 #include <algorithm>
 #include <cmath>
@@ -94,12 +95,6 @@ int check_config(const yb_config* c, int tp_size) {
   return 0;
 }
 
-// H2D copy of `rows` rows of `width` bytes from a host matrix with pitch spitch into a device
-// matrix with pitch dpitch.
-int copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t rows) {
-  YB_CK(cudaMemcpy2D(dst, dpitch, src, spitch, width, rows, cudaMemcpyHostToDevice));
-  return 0;
-}
 
 }  // namespace
 
@@ -107,18 +102,19 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
   const yb_config& c = e->cfg;
   const int r = e->tp_rank;
   const size_t dim = c.dim, hd = c.head_dim;
-  const size_t q_dim = (size_t)c.n_heads * hd, kv_dim = (size_t)c.n_kv_heads * hd;
+  const size_t q_dim = (size_t)c.n_heads * hd;
+  Loader ld;
   int rc;
+  if ((rc = ld.init())) return rc;
   if ((rc = dev_alloc(e, &e->emb, (size_t)c.vocab_size * dim * 2))) return rc;
-  YB_CK(cudaMemcpy(e->emb, w->token_embedding_table, (size_t)c.vocab_size * dim * 2, cudaMemcpyHostToDevice));
+  if ((rc = ld.contiguous(e->emb, w->token_embedding_table, (size_t)c.vocab_size * dim * 2))) return rc;
   if ((rc = dev_alloc(e, &e->rms_final, dim * 4))) return rc;
-  YB_CK(cudaMemcpy(e->rms_final, w->rms_final_weight, dim * 4, cudaMemcpyHostToDevice));
+  if ((rc = ld.contiguous(e->rms_final, w->rms_final_weight, dim * 4))) return rc;
   if (e->tp_size == 1 && w->wcls == w->token_embedding_table) {
     e->wcls = e->emb;  // tied embeddings
   } else {
     if ((rc = dev_alloc(e, &e->wcls, (size_t)e->vocab_l * dim * 2))) return rc;
-    YB_CK(cudaMemcpy(e->wcls, w->wcls + (size_t)r * e->vocab_l * dim, (size_t)e->vocab_l * dim * 2,
-                     cudaMemcpyHostToDevice));
+    if ((rc = ld.contiguous(e->wcls, w->wcls + (size_t)r * e->vocab_l * dim, (size_t)e->vocab_l * dim * 2))) return rc;
   }
   e->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -128,33 +124,43 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
       return set_error(YB_E_INVALID, "missing tensor for layer " + std::to_string(l));
     if ((rc = dev_alloc(e, &L.rms_att, dim * 4))) return rc;
     if ((rc = dev_alloc(e, &L.rms_ffn, dim * 4))) return rc;
-    YB_CK(cudaMemcpy(L.rms_att, w->rms_att_weight[l], dim * 4, cudaMemcpyHostToDevice));
-    YB_CK(cudaMemcpy(L.rms_ffn, w->rms_ffn_weight[l], dim * 4, cudaMemcpyHostToDevice));
+    if ((rc = ld.contiguous(L.rms_att, w->rms_att_weight[l], dim * 4))) return rc;
+    if ((rc = ld.contiguous(L.rms_ffn, w->rms_ffn_weight[l], dim * 4))) return rc;
     // [Wq rows of this rank's heads; Wk rows; Wv rows]
     const size_t qr = e->q_rows, kr = e->kv_rows;
     if ((rc = dev_alloc(e, &L.wqkv, (qr + 2 * kr) * dim * 2))) return rc;
-    YB_CK(cudaMemcpy(L.wqkv, w->wq[l] + (size_t)r * qr * dim, qr * dim * 2, cudaMemcpyHostToDevice));
-    YB_CK(cudaMemcpy(L.wqkv + qr * dim, w->wk[l] + (size_t)r * kr * dim, kr * dim * 2, cudaMemcpyHostToDevice));
-    YB_CK(cudaMemcpy(L.wqkv + (qr + kr) * dim, w->wv[l] + (size_t)r * kr * dim, kr * dim * 2, cudaMemcpyHostToDevice));
+    const uint16_t* wq = w->wq[l] + (size_t)r * qr * dim;
+    const uint16_t* wk = w->wk[l] + (size_t)r * kr * dim;
+    const uint16_t* wv = w->wv[l] + (size_t)r * kr * dim;
+    rc = ld.rows(L.wqkv, qr + 2 * kr, dim * 2, [=](size_t i) -> const void* {
+      return i < qr ? wq + i * dim : i < qr + kr ? wk + (i - qr) * dim : wv + (i - qr - kr) * dim;
+    });
+    if (rc) return rc;
     // Wo columns of this rank's heads
     if ((rc = dev_alloc(e, &L.wo, dim * qr * 2))) return rc;
-    if ((rc = copy2d(L.wo, qr * 2, w->wo[l] + (size_t)r * qr, q_dim * 2, qr * 2, dim))) return rc;
-    // W1 / W3 rows of this rank's hidden slice, interleaved
+    const uint16_t* wo = w->wo[l] + (size_t)r * qr;
+    if ((rc = ld.rows(L.wo, dim, qr * 2, [=](size_t i) -> const void* { return wo + i * q_dim; }))) return rc;
+    // W1 / W3 rows of this rank's hidden slice, interleaved (row 2i = W1 row i, 2i+1 = W3 row i)
     const size_t h = e->hid;
     if ((rc = dev_alloc(e, &L.w13, 2 * h * dim * 2))) return rc;
-    if ((rc = copy2d(L.w13, 2 * dim * 2, w->w1[l] + (size_t)r * h * dim, dim * 2, dim * 2, h))) return rc;
-    if ((rc = copy2d(L.w13 + dim, 2 * dim * 2, w->w3[l] + (size_t)r * h * dim, dim * 2, dim * 2, h))) return rc;
+    const uint16_t* w1 = w->w1[l] + (size_t)r * h * dim;
+    const uint16_t* w3 = w->w3[l] + (size_t)r * h * dim;
+    rc = ld.rows(L.w13, 2 * h, dim * 2, [=](size_t i) -> const void* { return ((i & 1) ? w3 : w1) + (i >> 1) * dim; });
+    if (rc) return rc;
     // W2 columns of the hidden slice
     if ((rc = dev_alloc(e, &L.w2, dim * h * 2))) return rc;
-    if ((rc = copy2d(L.w2, h * 2, w->w2[l] + (size_t)r * h, (size_t)c.hidden_dim * 2, h * 2, dim))) return rc;
+    const uint16_t* w2 = w->w2[l] + (size_t)r * h;
+    const size_t hid_full = (size_t)c.hidden_dim;
+    if ((rc = ld.rows(L.w2, dim, h * 2, [=](size_t i) -> const void* { return w2 + i * hid_full; }))) return rc;
     // KV cache, zero-initialised like yalm's (src/model.cpp:203-204)
     const size_t kvb = (size_t)e->nkv * c.max_seq_len * hd * 2;
     if ((rc = dev_alloc(e, &L.k_cache, kvb))) return rc;
     if ((rc = dev_alloc(e, &L.v_cache, kvb))) return rc;
     YB_CK(cudaMemset(L.k_cache, 0, kvb));
     YB_CK(cudaMemset(L.v_cache, 0, kvb));
-    (void)kv_dim;
   }
+  if ((rc = ld.finish())) return rc;
+  e->upload_bytes = ld.bytes();
   return 0;
 }
 

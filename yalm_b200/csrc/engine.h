@@ -103,6 +103,7 @@ struct yb_engine {
   unsigned* status_h = nullptr;  // host-mapped status word
   unsigned* status_d = nullptr;
   std::vector<void*> allocs;
+  size_t upload_bytes = 0;  // host bytes uploaded by yb_create
 
   yb::LaunchTuning tune;
   yb::GemvPlan plan_qkv{}, plan_wo{}, plan_gu{}, plan_w2{}, plan_cls{};
