@@ -39,11 +39,29 @@ sys.path.insert(0, ROOT)
 WORKLOADS = {"tiny": (32, 64), "mistral-7b": (16, 120), "llama-70b": (1024, 128)}
 PROMPT_LEN, DECODE_LEN = WORKLOADS["mistral-7b"]
 METRIC = "batch-1 decode tok/s (Mistral-7B fp16, 4k ctx)"
+METRICS = {"mistral-7b": METRIC, "tiny": "batch-1 decode tok/s (tiny Mistral-architecture fp16, ctx 1024)",
+           "llama-70b": "batch-1 decode tok/s (70B-class fp16, 8k ctx)"}
 FALLBACK_HBM_GBS = 6650.0
 
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
+
+
+class _StdoutToStderr:
+    """Sends file descriptor 1 to stderr for a while (NCCL prints its version banner on stdout when
+    a communicator is created; the bench's stdout carries only the JSON line)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
 
 
 def measured_peaks():
@@ -55,11 +73,11 @@ def measured_peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def model_file(config: str, rank: int, world: int, dist):
+def model_file(config: str, rank: int, world: int, dist, dtype: str = "fp16"):
     from yalm_b200 import synth
-    shape = synth.SHAPES[config]
+    shape = synth.shape_with(config, dtype=dtype)
     d = synth.scratch_dir(synth.file_bytes(shape))
-    path = os.path.join(d, f"yalm_{config}_seed0.yalm")
+    path = os.path.join(d, f"yalm_{config}_seed0.yalm" if dtype == "fp16" else f"yalm_{config}_{dtype}_seed0.yalm")
     if rank == 0:
         t = time.time()
         synth.write_yalm(path, shape, seed=0)
@@ -144,6 +162,9 @@ def run_reference(args):
         return 0
     from yalm_b200 import synth
     shape = synth.SHAPES[args.config]
+    if args.dtype != "fp16":
+        print(json.dumps({"impl": "reference", "unavailable": "yalm's runtime rejects fp8 checkpoints (src/model.cpp:61-70)"}))
+        return 0
     path = model_file(args.config, 0, 1, None)
     context = 8192 if args.config == "llama-70b" else 0
     # Each step is one full decode token of the reference; the sample is bounded to keep the run
@@ -159,7 +180,7 @@ def run_reference(args):
     sample = (f"{len(steps)} timed decode tokens (+{args.warmup} warm-up) of the full {args.config} model after a "
               f"2-token prompt, yalm -d cpu code path (Model::forward) via oracle/_ref/ref_decode")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRICS[args.config], "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
         "steps": len(steps), "warmup": args.warmup, "ms_per_step": round(1000 * t / len(steps), 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 weights, f32 compute",
         "data": "synthetic (seeded N(0,0.02) fp16 weights, random token ids)",
@@ -185,6 +206,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
     ap.add_argument("--no-long-context", action="store_true", help="skip the config-3 (3202-token prefill) phase")
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "fp8"],
+                    help="weight dtype of the synthetic checkpoint (fp8 = E5M2, as convert.py writes it)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     global PROMPT_LEN, DECODE_LEN
@@ -206,10 +229,11 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        with _StdoutToStderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+            dist.barrier()  # the communicator exists after the first collective
 
-    path = model_file(args.config, rank, world, dist)
+    path = model_file(args.config, rank, world, dist, args.dtype)
     context = 8192 if args.config == "llama-70b" else 0
     y = YALMData(path)
     t = time.time()
@@ -337,11 +361,12 @@ def main():
         names = ["qkv", "attention", "wo", "gateup", "w2", "classifier"]
         hid, dim = c.hidden_dim, c.dim
         q_dim, kv_dim = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
-        kbytes = {"qkv": (q_dim + 2 * kv_dim) * dim * 2 + dim * 8 + (q_dim + 2 * kv_dim) * 4,
-                  "wo": dim * q_dim * 2 + q_dim * 4 + dim * 8,
-                  "gateup": 2 * hid * dim * 2 + dim * 8 + hid * 4,
-                  "w2": dim * hid * 2 + hid * 4 + dim * 8,
-                  "classifier": c.vocab_size * dim * 2 + dim * 8 + c.vocab_size * 4}
+        wb = c.weight_bytes
+        kbytes = {"qkv": (q_dim + 2 * kv_dim) * dim * wb + dim * 8 + (q_dim + 2 * kv_dim) * 4,
+                  "wo": dim * q_dim * wb + q_dim * 4 + dim * 8,
+                  "gateup": 2 * hid * dim * wb + dim * 8 + hid * 4,
+                  "w2": dim * hid * wb + hid * 4 + dim * 8,
+                  "classifier": c.vocab_size * dim * wb + dim * 8 + c.vocab_size * 4}
         import ctypes
         for wi, nm in enumerate(names):
             msv = ctypes.c_float()
@@ -355,10 +380,11 @@ def main():
             traffic = None
             try:
                 with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-                    traffic = json.load(f).get(f"{args.config}:{dom}")
+                    traffic = json.load(f).get(f"{args.config}:{dom}" + ("" if args.dtype == "fp16" else f":{args.dtype}"))
             except Exception:
                 traffic = None
-            roofline = {"bound": "hbm", "kernel": f"gemv gate/up (fused W1/W3 + SwiGLU, {2 * hid}x{dim} fp16)",
+            roofline = {"bound": "hbm", "kernel": f"gemv gate/up (fused W1/W3 + SwiGLU, {2 * hid}x{dim} "
+                                                  f"{'fp16' if args.dtype == 'fp16' else 'fp8 E5M2'})",
                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
                         "fallback 6650 GB/s", "traffic": traffic,
@@ -369,7 +395,7 @@ def main():
         long_ctx = long_context(m, c, args, stream, world, dist, peak)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config != "llama-70b":
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config != "llama-70b" and args.dtype == "fp16":
         d = cpu_baseline(path, context, args.cpu_baseline_steps)
         if d:
             st = d["step_s"]
@@ -386,9 +412,11 @@ def main():
             launches_per_step = 1 + c.n_layers * (4 + m_w2_panels(m)) + 1 + (1 if world > 1 else 0)
         # the timed `value` region runs K logits-mode steps (no sampler kernel)
         out = {
-            "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRICS[args.config] if args.dtype == "fp16" else METRICS[args.config] + ", fp8 E5M2 weights",
+            "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_dev / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f16 weights, f32 accumulate/activations",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": ("f16" if args.dtype == "fp16" else "f8e5m2") + " weights, f32 accumulate/activations",
             "data": "synthetic (seeded N(0,0.02) fp16 weights in the .yalm layout, random token ids)",
             "config": {"workload": f"{args.config} batch-1 decode: {PROMPT_LEN}-token prompt, decode positions "
                                    f"{PROMPT_LEN}..{PROMPT_LEN + DECODE_LEN - 1}", "model": args.config,

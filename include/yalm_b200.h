@@ -37,8 +37,10 @@ extern "C" {
 #define YB_MODE_OUTPUT_LOGITS 1
 
 /* Config, src/model.h:56-82 (fields the decode path uses).  act: 0 = GELU, 1 = SILU
- * (ActivationType, src/model.h:19-22).  weight_dtype: 1 = F16 (DType order, src/codec.h:15-25);
- * only F16 is supported.  n_experts must be 0. */
+ * (ActivationType, src/model.h:19-22).  weight_dtype in yalm's DType order (src/codec.h:15-25):
+ * 1 = F16, or 3 = F8_E5M2 — the "fp8" dtype convert.py writes (convert.py:160, a plain cast to
+ * float8_e5m2), which yalm's own runtime rejects (src/model.cpp:61-70); each E5M2 weight is the top
+ * byte of the fp16 with the same value.  n_experts must be 0. */
 typedef struct yb_config {
   int dim;
   int hidden_dim;
@@ -58,8 +60,9 @@ typedef struct yb_config {
 } yb_config;
 
 /* Host pointers to the tensors `Model` / `Block` hold before `cuda()` (src/model.h:249-264,
- * 276-281); per-layer arrays have n_layers entries.  Matrices are fp16 row-major exactly as in
- * the .yalm file.  wcls may equal token_embedding_table (tied embeddings, src/model.cpp:425-434). */
+ * 276-281); per-layer arrays have n_layers entries.  Matrices are row-major exactly as in the .yalm
+ * file: fp16 values, or for weight_dtype 3 one-byte E5M2 values (the pointers are then cast).  wcls
+ * may equal token_embedding_table (tied embeddings, src/model.cpp:425-434). */
 typedef struct yb_weights {
   const uint16_t* token_embedding_table; /* [vocab_size, dim] */
   const float* rms_final_weight;         /* [dim] */

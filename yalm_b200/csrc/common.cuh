@@ -206,6 +206,28 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
   return v[0];
 }
 
+// 16 fp8 E5M2 weights (one 16-byte vector) dotted with 16 fp32 activations.  An E5M2 value is
+// the top byte of the fp16 with the same value, so a byte permute that puts each byte above a zero
+// byte yields two fp16 values per 32-bit word, exactly; two FMA chains as in dot8.
+__device__ __forceinline__ float dot16_e5m2(uint4 w, const float4& x0, const float4& x1, const float4& x2,
+                                            const float4& x3) {
+  const unsigned q[4] = {w.x, w.y, w.z, w.w};
+  const float4* xs[4] = {&x0, &x1, &x2, &x3};
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const unsigned lo = __byte_perm(q[i], 0u, 0x1404u);  // elements 4i, 4i+1 as fp16
+    const unsigned hi = __byte_perm(q[i], 0u, 0x3424u);  // elements 4i+2, 4i+3
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+    a0 = fmaf(f0.x, xs[i]->x, a0);
+    a1 = fmaf(f0.y, xs[i]->y, a1);
+    a0 = fmaf(f1.x, xs[i]->z, a0);
+    a1 = fmaf(f1.y, xs[i]->w, a1);
+  }
+  return a0 + a1;
+}
+
 // 8 fp16 weights (one 16-byte vector) dotted with 8 fp32 activations: two independent 4-long FMA
 // chains (even / odd elements), so the dependency chain is half as long.
 __device__ __forceinline__ float dot8(uint4 w, const float4& xa, const float4& xb) {

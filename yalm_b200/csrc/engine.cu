@@ -49,10 +49,17 @@ __global__ void step_kernel(const StepArgs a) {
     *a.step = s;
   }
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n_bar; i += gridDim.x * blockDim.x) a.bar[i] = 0u;
-  // embedding row -> fp32 residual stream (src/infer.cpp:460-481)
-  const __half* row = a.emb + (size_t)a.token * a.dim;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.dim; i += gridDim.x * blockDim.x)
-    a.x[i] = __half2float(row[i]);
+  // embedding row -> fp32 residual stream (src/infer.cpp:460-481); an fp8 E5M2 value is the top
+  // byte of the fp16 with the same value
+  if (a.esz == 1) {
+    const unsigned char* row = reinterpret_cast<const unsigned char*>(a.emb) + (size_t)a.token * a.dim;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.dim; i += gridDim.x * blockDim.x)
+      a.x[i] = __half2float(__ushort_as_half((unsigned short)(row[i] << 8)));
+  } else {
+    const __half* row = a.emb + (size_t)a.token * a.dim;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.dim; i += gridDim.x * blockDim.x)
+      a.x[i] = __half2float(row[i]);
+  }
 }
 
 // Kernel that waits (bounded) for every rank's slice of the gathered logits.
@@ -77,7 +84,8 @@ int dev_alloc(yb_engine* e, T** p, size_t bytes) {
 
 int check_config(const yb_config* c, int tp_size) {
   if (!c) return set_error(YB_E_INVALID, "null config");
-  if (c->weight_dtype != 1) return set_error(YB_E_UNSUPPORTED, "only fp16 weights (dtype F16) are supported");
+  if (c->weight_dtype != 1 && c->weight_dtype != 3)
+    return set_error(YB_E_UNSUPPORTED, "weights must be fp16 (dtype F16) or fp8 E5M2 (dtype F8_E5M2)");
   if (c->n_experts != 0) return set_error(YB_E_UNSUPPORTED, "mixture-of-experts checkpoints are not supported");
   if (c->dim <= 0 || c->hidden_dim <= 0 || c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 ||
       c->vocab_size <= 0 || c->max_seq_len <= 2)
@@ -90,8 +98,11 @@ int check_config(const yb_config* c, int tp_size) {
     return set_error(YB_E_INVALID, "rotary_dim must be even and <= head_dim");
   if (c->dim % 8 || c->hidden_dim % 8) return set_error(YB_E_UNSUPPORTED, "dim and hidden_dim must be multiples of 8");
   if (c->act != 0 && c->act != 1) return set_error(YB_E_INVALID, "act must be 0 (gelu) or 1 (silu)");
-  if (tp_size < 1 || c->n_kv_heads % tp_size || c->hidden_dim % (8 * tp_size) || c->vocab_size % tp_size)
-    return set_error(YB_E_INVALID, "tp_size must divide n_kv_heads, vocab_size and hidden_dim/8");
+  const int cm = c->weight_dtype == 3 ? 16 : 8;  // weights per 16-byte chunk
+  if (c->dim % cm || c->hidden_dim % cm || (c->n_heads * c->head_dim) % cm)
+    return set_error(YB_E_UNSUPPORTED, "fp8 weights need dim and hidden_dim multiples of 16");
+  if (tp_size < 1 || c->n_kv_heads % tp_size || c->hidden_dim % (cm * tp_size) || c->vocab_size % tp_size)
+    return set_error(YB_E_INVALID, "tp_size must divide n_kv_heads, vocab_size and hidden_dim/8 (/16 for fp8)");
   return 0;
 }
 
@@ -103,18 +114,21 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
   const int r = e->tp_rank;
   const size_t dim = c.dim, hd = c.head_dim;
   const size_t q_dim = (size_t)c.n_heads * hd;
+  const size_t es = e->esz;  // bytes per weight
+  auto bytes = [](const void* p) { return static_cast<const unsigned char*>(p); };
   Loader ld;
   int rc;
   if ((rc = ld.init())) return rc;
-  if ((rc = dev_alloc(e, &e->emb, (size_t)c.vocab_size * dim * 2))) return rc;
-  if ((rc = ld.contiguous(e->emb, w->token_embedding_table, (size_t)c.vocab_size * dim * 2))) return rc;
+  if ((rc = dev_alloc(e, &e->emb, (size_t)c.vocab_size * dim * es))) return rc;
+  if ((rc = ld.contiguous(e->emb, w->token_embedding_table, (size_t)c.vocab_size * dim * es))) return rc;
   if ((rc = dev_alloc(e, &e->rms_final, dim * 4))) return rc;
   if ((rc = ld.contiguous(e->rms_final, w->rms_final_weight, dim * 4))) return rc;
   if (e->tp_size == 1 && w->wcls == w->token_embedding_table) {
     e->wcls = e->emb;  // tied embeddings
   } else {
-    if ((rc = dev_alloc(e, &e->wcls, (size_t)e->vocab_l * dim * 2))) return rc;
-    if ((rc = ld.contiguous(e->wcls, w->wcls + (size_t)r * e->vocab_l * dim, (size_t)e->vocab_l * dim * 2))) return rc;
+    if ((rc = dev_alloc(e, &e->wcls, (size_t)e->vocab_l * dim * es))) return rc;
+    if ((rc = ld.contiguous(e->wcls, bytes(w->wcls) + (size_t)r * e->vocab_l * dim * es, (size_t)e->vocab_l * dim * es)))
+      return rc;
   }
   e->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -128,30 +142,31 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
     if ((rc = ld.contiguous(L.rms_ffn, w->rms_ffn_weight[l], dim * 4))) return rc;
     // [Wq rows of this rank's heads; Wk rows; Wv rows]
     const size_t qr = e->q_rows, kr = e->kv_rows;
-    if ((rc = dev_alloc(e, &L.wqkv, (qr + 2 * kr) * dim * 2))) return rc;
-    const uint16_t* wq = w->wq[l] + (size_t)r * qr * dim;
-    const uint16_t* wk = w->wk[l] + (size_t)r * kr * dim;
-    const uint16_t* wv = w->wv[l] + (size_t)r * kr * dim;
-    rc = ld.rows(L.wqkv, qr + 2 * kr, dim * 2, [=](size_t i) -> const void* {
-      return i < qr ? wq + i * dim : i < qr + kr ? wk + (i - qr) * dim : wv + (i - qr - kr) * dim;
+    if ((rc = dev_alloc(e, &L.wqkv, (qr + 2 * kr) * dim * es))) return rc;
+    const unsigned char* wq = bytes(w->wq[l]) + (size_t)r * qr * dim * es;
+    const unsigned char* wk = bytes(w->wk[l]) + (size_t)r * kr * dim * es;
+    const unsigned char* wv = bytes(w->wv[l]) + (size_t)r * kr * dim * es;
+    const size_t rb = dim * es;  // bytes per row of a dim-wide matrix
+    rc = ld.rows(L.wqkv, qr + 2 * kr, rb, [=](size_t i) -> const void* {
+      return i < qr ? wq + i * rb : i < qr + kr ? wk + (i - qr) * rb : wv + (i - qr - kr) * rb;
     });
     if (rc) return rc;
     // Wo columns of this rank's heads
-    if ((rc = dev_alloc(e, &L.wo, dim * qr * 2))) return rc;
-    const uint16_t* wo = w->wo[l] + (size_t)r * qr;
-    if ((rc = ld.rows(L.wo, dim, qr * 2, [=](size_t i) -> const void* { return wo + i * q_dim; }))) return rc;
+    if ((rc = dev_alloc(e, &L.wo, dim * qr * es))) return rc;
+    const unsigned char* wo = bytes(w->wo[l]) + (size_t)r * qr * es;
+    if ((rc = ld.rows(L.wo, dim, qr * es, [=](size_t i) -> const void* { return wo + i * q_dim * es; }))) return rc;
     // W1 / W3 rows of this rank's hidden slice, interleaved (row 2i = W1 row i, 2i+1 = W3 row i)
     const size_t h = e->hid;
-    if ((rc = dev_alloc(e, &L.w13, 2 * h * dim * 2))) return rc;
-    const uint16_t* w1 = w->w1[l] + (size_t)r * h * dim;
-    const uint16_t* w3 = w->w3[l] + (size_t)r * h * dim;
-    rc = ld.rows(L.w13, 2 * h, dim * 2, [=](size_t i) -> const void* { return ((i & 1) ? w3 : w1) + (i >> 1) * dim; });
+    if ((rc = dev_alloc(e, &L.w13, 2 * h * dim * es))) return rc;
+    const unsigned char* w1 = bytes(w->w1[l]) + (size_t)r * h * rb;
+    const unsigned char* w3 = bytes(w->w3[l]) + (size_t)r * h * rb;
+    rc = ld.rows(L.w13, 2 * h, rb, [=](size_t i) -> const void* { return ((i & 1) ? w3 : w1) + (i >> 1) * rb; });
     if (rc) return rc;
     // W2 columns of the hidden slice
-    if ((rc = dev_alloc(e, &L.w2, dim * h * 2))) return rc;
-    const uint16_t* w2 = w->w2[l] + (size_t)r * h;
-    const size_t hid_full = (size_t)c.hidden_dim;
-    if ((rc = ld.rows(L.w2, dim, h * 2, [=](size_t i) -> const void* { return w2 + i * hid_full; }))) return rc;
+    if ((rc = dev_alloc(e, &L.w2, dim * h * es))) return rc;
+    const unsigned char* w2 = bytes(w->w2[l]) + (size_t)r * h * es;
+    const size_t hid_row = (size_t)c.hidden_dim * es;
+    if ((rc = ld.rows(L.w2, dim, h * es, [=](size_t i) -> const void* { return w2 + i * hid_row; }))) return rc;
     // KV cache, zero-initialised like yalm's (src/model.cpp:203-204)
     const size_t kvb = (size_t)e->nkv * c.max_seq_len * hd * 2;
     if ((rc = dev_alloc(e, &L.k_cache, kvb))) return rc;
@@ -168,6 +183,11 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
 static const unsigned long long* tp_in(yb_engine* e, int pt) {
   return reinterpret_cast<const unsigned long long*>(static_cast<char*>(e->tp.base) + e->tp.x_off) +
          (size_t)pt * e->tp_size * e->cfg.dim;
+}
+
+// Matrix pointer `cols` weights into each row (a column panel), for either weight type.
+static const __half* wcols(const yb_engine* e, const __half* base, size_t cols) {
+  return reinterpret_cast<const __half*>(reinterpret_cast<const unsigned char*>(base) + cols * e->esz);
 }
 
 static GemvArgs base_args(yb_engine* e) {
@@ -243,7 +263,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       }
       if (e->tune.prefetch_wo) {
         a.pf_src = reinterpret_cast<const unsigned char*>(L.wo);
-        a.pf_bytes = (long long)c.dim * e->q_rows * 2;
+        a.pf_bytes = (long long)c.dim * e->q_rows * e->esz;
       }
       timeline(&a.trace, &a.trace_stride);
       YB_CK(gemv_launch(a.tp_ll ? e->plan_qkv_tp : e->plan_qkv, a, s, true, pf));
@@ -307,7 +327,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       const int pcols = e->hid / panels;
       for (int p = 0; p < panels; ++p) {
         GemvArgs a = base_args(e);
-        a.w = L.w2 + (size_t)p * pcols;
+        a.w = wcols(e, L.w2, (size_t)p * pcols);
         a.ldw = e->hid;
         a.rows = c.dim;
         a.cols = pcols;
@@ -319,7 +339,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
         }
         if (e->tune.prefetch_qkv && p == panels - 1 && l + 1 < c.n_layers) {
           a.pf_src = reinterpret_cast<const unsigned char*>(e->layers[l + 1].wqkv);
-          a.pf_bytes = (long long)(e->q_rows + 2 * e->kv_rows) * c.dim * 2;
+          a.pf_bytes = (long long)(e->q_rows + 2 * e->kv_rows) * c.dim * e->esz;
         }
         timeline(&a.trace, &a.trace_stride);
         YB_CK(gemv_launch(e->plan_w2, a, s, true, pf));
@@ -376,7 +396,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
 
 static int build_graph(yb_engine* e, int mode) {
   StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, 0, 0, e->cfg.max_seq_len, 0, 0, 0, 0, 0.f, 0.f,
-              e->tp.d_bar, e->tp.d_bar ? 2 * e->cfg.n_layers : 0};
+              e->tp.d_bar, e->tp.d_bar ? 2 * e->cfg.n_layers : 0, e->esz};
   cudaGraph_t g = nullptr;
   YB_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
   int rc = record_step(e, mode, sa);
@@ -412,6 +432,7 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
   if (!w) return set_error(YB_E_INVALID, "null weights");
   if (tp_rank < 0 || tp_rank >= tp_size) return set_error(YB_E_INVALID, "tp_rank out of range");
   e->cfg = *cfg;
+  e->esz = cfg->weight_dtype == 3 ? 1 : 2;
   e->tune = LaunchTuning::from_env();
   e->device = device;
   e->tp_rank = tp_rank;
@@ -456,18 +477,19 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
 
   // kernel plans
   const int epi_res = tp_size > 1 ? kEpiResidTP : kEpiResid;
-  e->plan_qkv = gemv_plan(e->q_rows + 2 * e->kv_rows, c.dim, kEpiQKV, true, e->n_sms, e->tune);
-  e->plan_wo = gemv_plan(c.dim, e->q_rows, epi_res, false, e->n_sms, e->tune);
-  e->plan_gu = gemv_plan(2 * e->hid, c.dim, kEpiGateUp, true, e->n_sms, e->tune, tp_size > 1);
-  e->plan_qkv_tp = tp_size > 1 ? gemv_plan(e->q_rows + 2 * e->kv_rows, c.dim, kEpiQKV, true, e->n_sms, e->tune, true)
+  e->plan_qkv = gemv_plan(e->q_rows + 2 * e->kv_rows, c.dim, kEpiQKV, true, e->n_sms, e->tune, false, e->esz);
+  e->plan_wo = gemv_plan(c.dim, e->q_rows, epi_res, false, e->n_sms, e->tune, false, e->esz);
+  e->plan_gu = gemv_plan(2 * e->hid, c.dim, kEpiGateUp, true, e->n_sms, e->tune, tp_size > 1, e->esz);
+  e->plan_qkv_tp = tp_size > 1 ? gemv_plan(e->q_rows + 2 * e->kv_rows, c.dim, kEpiQKV, true, e->n_sms, e->tune, true, e->esz)
                                : e->plan_qkv;
   e->w2_panels = 1;
-  while (gemv_kpt_for(e->hid / e->w2_panels) < 0 || (e->hid / e->w2_panels) % 8 || e->hid % e->w2_panels) {
+  const int col_mult = e->esz == 1 ? 16 : 8;  // columns per 16-byte chunk
+  while (gemv_kpt_for(e->hid / e->w2_panels, e->esz) < 0 || (e->hid / e->w2_panels) % col_mult || e->hid % e->w2_panels) {
     if (++e->w2_panels > 16) return set_error(YB_E_UNSUPPORTED, "hidden_dim too large");
   }
   if (tp_size > 1 && e->w2_panels > 1) return set_error(YB_E_UNSUPPORTED, "hidden_dim per rank too large for tensor parallelism");
-  e->plan_w2 = gemv_plan(c.dim, e->hid / e->w2_panels, epi_res, false, e->n_sms, e->tune);
-  e->plan_cls = gemv_plan(e->vocab_l, c.dim, tp_size > 1 ? kEpiStoreTP : kEpiStore, true, e->n_sms, e->tune, tp_size > 1);
+  e->plan_w2 = gemv_plan(c.dim, e->hid / e->w2_panels, epi_res, false, e->n_sms, e->tune, false, e->esz);
+  e->plan_cls = gemv_plan(e->vocab_l, c.dim, tp_size > 1 ? kEpiStoreTP : kEpiStore, true, e->n_sms, e->tune, tp_size > 1, e->esz);
   e->plan_attn = attn_plan(e->nh, e->nkv, c.head_dim, c.max_seq_len);
   if (!e->plan_qkv.ok || !e->plan_qkv_tp.ok || !e->plan_wo.ok || !e->plan_gu.ok || !e->plan_w2.ok ||
       !e->plan_cls.ok || !e->plan_attn.ok)
@@ -481,7 +503,7 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
     const bool want = ex && std::string(ex) == "persistent";
     int coop = 0;
     YB_CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
-    if (want && coop && tp_size == 1) {
+    if (want && coop && tp_size == 1 && e->esz == 2) {
       PersistPlan pp = persist_plan(c.dim, e->q_rows, e->hid, c.head_dim, c.n_heads / c.n_kv_heads, e->n_sms);
       if (pp.ok) {
         const int G = pp.grid;
@@ -654,7 +676,7 @@ static int launch_step(yb_engine* e, int token, int pos, int mode, const SampleP
   }
   StepArgs sa{e->step, e->x, e->emb, e->cfg.dim, token, pos, e->cfg.max_seq_len, e->epoch, e->lepoch,
               sp ? sp->op : 0, sp ? sp->target : 0, sp ? sp->temperature : 0.f, sp ? sp->coin : 0.f,
-              e->tp.d_bar, e->tp.d_bar ? 2 * e->cfg.n_layers : 0};
+              e->tp.d_bar, e->tp.d_bar ? 2 * e->cfg.n_layers : 0, e->esz};
   cudaKernelNodeParams kp = {};
   void* params[] = {&sa};
   kp.func = reinterpret_cast<void*>(&step_kernel);
@@ -854,7 +876,7 @@ extern "C" int yb_profile_kernel(yb_engine* e, int which, int iters, float* ms_p
         const int pcols = e->hid / e->w2_panels;
         for (int p = 0; p < e->w2_panels; ++p) {
           GemvArgs h = base_args(e);
-          h.w = L.w2 + (size_t)p * pcols; h.ldw = e->hid; h.rows = c.dim; h.cols = pcols;
+          h.w = wcols(e, L.w2, (size_t)p * pcols); h.ldw = e->hid; h.rows = c.dim; h.cols = pcols;
           h.x = e->hb + (size_t)p * pcols; h.y = e->x;
           YB_CK(gemv_launch(e->plan_w2, h, e->stream, true, pf));
         }

@@ -70,6 +70,7 @@ struct StepArgs {
   float coin;
   unsigned* bar;  // counters the step kernel zeroes (tensor-parallel barriers), n_bar of them
   int n_bar;
+  int esz;  // bytes per weight: 2 fp16, 1 fp8 E5M2
 };
 
 // Graph / launch variants of a step: the two InferenceModes, and logits followed by the sampler.
@@ -83,6 +84,7 @@ struct yb_engine {
   cudaStream_t stream = nullptr;
   yb_config cfg{};
   int tp_rank = 0, tp_size = 1;
+  int esz = 2;  // bytes per weight: 2 fp16, 1 fp8 E5M2 (device matrices hold that many bytes per element)
   // local (this rank's) shapes
   int nh = 0, nkv = 0, q_rows = 0, kv_rows = 0, hid = 0, vocab_l = 0;
 

@@ -11,10 +11,14 @@ namespace yb {
 // IN: 0 = x as given, 1 = RMS-normalised x, 2 = RMS-normalised x plus the tensor-parallel partial
 // sums of the previous row-parallel matvec (GemvArgs::tp_ll).  Only IN == 2 instances carry the
 // exchange-read code, so the others keep their registers for the stream loop.
-template <int NW, int KPT, int RT, int EPI, int IN>
+// WT: weight type, 0 = fp16, 1 = fp8 E5M2 (the top byte of an fp16).  A 16-byte chunk of a row holds
+// EPC = 8 or 16 weights; thread t owns the chunks t, t + NT, ... and the matching EPC values of x.
+template <int NW, int KPT, int RT, int EPI, int IN, int WT>
 __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a) {
   constexpr bool NORM = IN >= 1;
   constexpr bool TPIN = IN == 2;
+  constexpr int EPC = WT ? 16 : 8;  // weights (and x values) per 16-byte chunk
+  constexpr int V = EPC / 4;        // float4 of x per chunk
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -32,7 +36,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
   const int NS = a.n_slots;
   const unsigned SB = a.stage_bytes;
   const int C = a.cols;
-  const unsigned row_bytes = (unsigned)C * 2u;
+  const unsigned row_bytes = (unsigned)C * (WT ? 1u : 2u);
 
   unsigned char* ring = smem;
   float* red = reinterpret_cast<float*>(smem + (size_t)NS * SB);
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
         bulk_g2s(dst, wbase + (size_t)row0 * row_bytes, (unsigned)nr * row_bytes, &full[slot], pol);
       } else {
         for (int r = 0; r < nr; ++r)
-          bulk_g2s(dst + (size_t)r * row_bytes, wbase + (size_t)(row0 + r) * (size_t)a.ldw * 2u, row_bytes,
+          bulk_g2s(dst + (size_t)r * row_bytes, wbase + (size_t)(row0 + r) * (size_t)a.ldw * (WT ? 1u : 2u), row_bytes,
                    &full[slot], pol);
       }
       issued = i + 1;
@@ -125,16 +129,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
 
   // -------------------------------------------------------------------- consumers
   const int t = threadIdx.x;  // 0 .. NT-1
-  const int n_chunks = C >> 3;
-  float4 xr[KPT][2];
-  float4 nw[NORM ? KPT : 1][2];
+  const int n_chunks = C / EPC;
+  float4 xr[KPT][V];
+  float4 nw[NORM ? KPT : 1][V];
   if (NORM) {
 #pragma unroll
     for (int k = 0; k < KPT; ++k) {
       const int c = k * NT + t;
       if (c < n_chunks) {
-        nw[k][0] = __ldg(reinterpret_cast<const float4*>(a.norm_w) + 2 * c);
-        nw[k][1] = __ldg(reinterpret_cast<const float4*>(a.norm_w) + 2 * c + 1);
+#pragma unroll
+        for (int v = 0; v < V; ++v) nw[k][v] = __ldg(reinterpret_cast<const float4*>(a.norm_w) + V * c + v);
       }
     }
   }
@@ -154,7 +158,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
     const int w_begin = (int)((long long)n_chunks * blockIdx.x / G);
     const int w_end = (int)((long long)n_chunks * (blockIdx.x + 1) / G);
     bool ok = true;
-    for (int e = w_begin * 8 + t; e < w_end * 8; e += NT) {
+    for (int e = w_begin * EPC + t; e < w_end * EPC; e += NT) {
       float v = a.x[e];
       for (int r0 = 0; r0 < a.tp_size && ok; r0 += 8) {
         const int nr = min(8, a.tp_size - r0);
@@ -212,17 +216,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
 #pragma unroll
   for (int k = 0; k < KPT; ++k) {
     const int c = k * NT + t;
-    if (c < n_chunks) {
-      if (TPIN && a.tp_ll) {  // written by other CTAs of this kernel: read through L2
-        xr[k][0] = __ldcg(reinterpret_cast<const float4*>(xin) + 2 * c);
-        xr[k][1] = __ldcg(reinterpret_cast<const float4*>(xin) + 2 * c + 1);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      if (c < n_chunks) {
+        if (TPIN && a.tp_ll)  // written by other CTAs of this kernel: read through L2
+          xr[k][v] = __ldcg(reinterpret_cast<const float4*>(xin) + V * c + v);
+        else
+          xr[k][v] = reinterpret_cast<const float4*>(xin)[V * c + v];
       } else {
-        xr[k][0] = reinterpret_cast<const float4*>(xin)[2 * c];
-        xr[k][1] = reinterpret_cast<const float4*>(xin)[2 * c + 1];
+        xr[k][v] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    } else {
-      xr[k][0] = make_float4(0.f, 0.f, 0.f, 0.f);
-      xr[k][1] = xr[k][0];
     }
   }
   if (t == 0) timeline_stamp(a.trace, a.trace_stride, 1);
@@ -230,10 +233,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
     // RMSNorm (yalm src/infer.cpp:136-146): scale = 1 / sqrt(mean(x^2) + eps); x * scale * w
     float ss = 0.f;
 #pragma unroll
-    for (int k = 0; k < KPT; ++k) {
-      ss += xr[k][0].x * xr[k][0].x + xr[k][0].y * xr[k][0].y + xr[k][0].z * xr[k][0].z + xr[k][0].w * xr[k][0].w;
-      ss += xr[k][1].x * xr[k][1].x + xr[k][1].y * xr[k][1].y + xr[k][1].z * xr[k][1].z + xr[k][1].w * xr[k][1].w;
-    }
+    for (int k = 0; k < KPT; ++k)
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        ss += xr[k][v].x * xr[k][v].x + xr[k][v].y * xr[k][v].y + xr[k][v].z * xr[k][v].z + xr[k][v].w * xr[k][v].w;
     ss = warp_sum(ss);
     if (lane == 0) scratch[warp] = ss;
     named_sync(1, NT);
@@ -246,14 +249,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
     for (int k = 0; k < KPT; ++k) {
       const int c = k * NT + t;
       if (c < n_chunks) {
-        xr[k][0].x = xr[k][0].x * scale * nw[k][0].x;
-        xr[k][0].y = xr[k][0].y * scale * nw[k][0].y;
-        xr[k][0].z = xr[k][0].z * scale * nw[k][0].z;
-        xr[k][0].w = xr[k][0].w * scale * nw[k][0].w;
-        xr[k][1].x = xr[k][1].x * scale * nw[k][1].x;
-        xr[k][1].y = xr[k][1].y * scale * nw[k][1].y;
-        xr[k][1].z = xr[k][1].z * scale * nw[k][1].z;
-        xr[k][1].w = xr[k][1].w * scale * nw[k][1].w;
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          xr[k][v].x = xr[k][v].x * scale * nw[k][v].x;
+          xr[k][v].y = xr[k][v].y * scale * nw[k][v].y;
+          xr[k][v].z = xr[k][v].z * scale * nw[k][v].z;
+          xr[k][v].w = xr[k][v].w * scale * nw[k][v].w;
+        }
       }
     }
   }
@@ -280,7 +282,12 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
       }
       float part[KPT];
 #pragma unroll
-      for (int k = 0; k < KPT; ++k) part[k] = dot8(wv[k], xr[k][0], xr[k][1]);
+      for (int k = 0; k < KPT; ++k) {
+        if (WT)
+          part[k] = dot16_e5m2(wv[k], xr[k][0], xr[k][1], xr[k][V > 2 ? 2 : 0], xr[k][V > 2 ? 3 : 1]);
+        else
+          part[k] = dot8(wv[k], xr[k][0], xr[k][1]);
+      }
       float s = part[0];
 #pragma unroll
       for (int k = 1; k < KPT; ++k) s += part[k];
@@ -405,51 +412,61 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a
 // ---------------------------------------------------------------------------------- host side
 namespace {
 
-template <int KPT, int RT, int EPI, int IN>
+template <int KPT, int RT, int EPI, int IN, int WT>
 const void* pick4() {
-  return reinterpret_cast<const void*>(&gemv_kernel<kGemvWarps, KPT, RT, EPI, IN>);
+  return reinterpret_cast<const void*>(&gemv_kernel<kGemvWarps, KPT, RT, EPI, IN, WT>);
 }
 // Instantiated combinations: residual epilogues never normalise their input; the tensor-parallel
 // logits epilogue always does; pair epilogues (gate/up, QKV) need at least two rows per stage; the
 // tensor-parallel input (in == 2) exists for the normalised dim-wide inputs (KPT <= 4, dim <= 8192)
 // of the QKV, gate/up and logits matvecs.
-template <int KPT, int RT>
+template <int KPT, int RT, int WT>
 const void* pick2(int epi, int in) {
   constexpr int RP = RT >= 2 ? RT : 2;
   constexpr bool TPK = KPT <= 4;
   switch (epi) {
     case kEpiStore:
-      return in == 0 ? pick4<KPT, RT, kEpiStore, 0>() : in == 1 ? pick4<KPT, RT, kEpiStore, 1>() : nullptr;
-    case kEpiResid: return in == 0 ? pick4<KPT, RT, kEpiResid, 0>() : nullptr;
+      return in == 0 ? pick4<KPT, RT, kEpiStore, 0, WT>() : in == 1 ? pick4<KPT, RT, kEpiStore, 1, WT>() : nullptr;
+    case kEpiResid: return in == 0 ? pick4<KPT, RT, kEpiResid, 0, WT>() : nullptr;
     case kEpiGateUp:
       if (RT < 2) return nullptr;
-      if (in == 2) return TPK ? pick4<KPT, RP, kEpiGateUp, TPK ? 2 : 1>() : nullptr;
-      return in == 1 ? pick4<KPT, RP, kEpiGateUp, 1>() : pick4<KPT, RP, kEpiGateUp, 0>();
+      if (in == 2) return TPK ? pick4<KPT, RP, kEpiGateUp, TPK ? 2 : 1, WT>() : nullptr;
+      return in == 1 ? pick4<KPT, RP, kEpiGateUp, 1, WT>() : pick4<KPT, RP, kEpiGateUp, 0, WT>();
     case kEpiQKV:
       if (RT < 2) return nullptr;
-      if (in == 2) return TPK ? pick4<KPT, RP, kEpiQKV, TPK ? 2 : 1>() : nullptr;
-      return in == 1 ? pick4<KPT, RP, kEpiQKV, 1>() : pick4<KPT, RP, kEpiQKV, 0>();
-    case kEpiResidTP: return in == 0 ? pick4<KPT, RT, kEpiResidTP, 0>() : nullptr;
-    case kEpiStoreTP: return in == 2 && TPK ? pick4<KPT, RT, kEpiStoreTP, TPK ? 2 : 1>() : nullptr;
+      if (in == 2) return TPK ? pick4<KPT, RP, kEpiQKV, TPK ? 2 : 1, WT>() : nullptr;
+      return in == 1 ? pick4<KPT, RP, kEpiQKV, 1, WT>() : pick4<KPT, RP, kEpiQKV, 0, WT>();
+    case kEpiResidTP: return in == 0 ? pick4<KPT, RT, kEpiResidTP, 0, WT>() : nullptr;
+    case kEpiStoreTP: return in == 2 && TPK ? pick4<KPT, RT, kEpiStoreTP, TPK ? 2 : 1, WT>() : nullptr;
   }
   return nullptr;
 }
-template <int KPT>
+template <int KPT, int WT>
 const void* pick1(int rt, int epi, int in) {
   switch (rt) {
-    case 1: return pick2<KPT, 1>(epi, in);
-    case 2: return pick2<KPT, 2>(epi, in);
-    case 4: return pick2<KPT, 4>(epi, in);
-    case 8: return pick2<KPT, 8>(epi, in);
+    case 1: return pick2<KPT, 1, WT>(epi, in);
+    case 2: return pick2<KPT, 2, WT>(epi, in);
+    case 4: return pick2<KPT, 4, WT>(epi, in);
+    case 8: return pick2<KPT, 8, WT>(epi, in);
   }
   return nullptr;
 }
-const void* pick(int kpt, int rt, int epi, int in) {
-  switch (kpt) {
-    case 1: return pick1<1>(rt, epi, in);
-    case 2: return pick1<2>(rt, epi, in);
-    case 4: return pick1<4>(rt, epi, in);
-    case 7: return pick1<7>(rt, epi, in);
+// fp8 rows hold twice the chunks' worth of weights: KPT 7 is not instantiated for them (it would
+// mean more than 28672 columns).
+const void* pick(int kpt, int rt, int epi, int in, int wt) {
+  if (wt == 0) {
+    switch (kpt) {
+      case 1: return pick1<1, 0>(rt, epi, in);
+      case 2: return pick1<2, 0>(rt, epi, in);
+      case 4: return pick1<4, 0>(rt, epi, in);
+      case 7: return pick1<7, 0>(rt, epi, in);
+    }
+  } else {
+    switch (kpt) {
+      case 1: return pick1<1, 1>(rt, epi, in);
+      case 2: return pick1<2, 1>(rt, epi, in);
+      case 4: return pick1<4, 1>(rt, epi, in);
+    }
   }
   return nullptr;
 }
@@ -488,23 +505,24 @@ LaunchTuning LaunchTuning::from_env() {
   return cached;
 }
 
-int gemv_kpt_for(int cols) {
-  const int chunks = cols / 8;
+int gemv_kpt_for(int cols, int esz) {
+  const int chunks = cols / (esz == 1 ? 16 : 8);
   const int per = (chunks + kGemvWarps * 32 - 1) / (kGemvWarps * 32);
   if (per <= 1) return 1;
   if (per <= 2) return 2;
   if (per <= 4) return 4;
-  if (per <= 7) return 7;
+  if (per <= 7 && esz == 2) return 7;  // fp8 rows stop at KPT 4 (the caller splits wider matrices)
   return -1;
 }
 
-GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune, bool tp_in) {
+GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune, bool tp_in, int esz) {
   GemvPlan p{};
   p.ok = false;
-  if (cols <= 0 || rows <= 0 || (cols % 8) != 0) return p;
-  p.kpt = gemv_kpt_for(cols);
+  if (esz != 1 && esz != 2) return p;
+  if (cols <= 0 || rows <= 0 || (cols % (esz == 1 ? 16 : 8)) != 0) return p;
+  p.kpt = gemv_kpt_for(cols, esz);
   if (p.kpt < 0) return p;
-  const int row_bytes = cols * 2;
+  const int row_bytes = cols * esz;
   int rt = 1;
   while (rt < 8 && (rt * 2) * row_bytes <= tune.stage_bytes_target) rt *= 2;
   const bool pairs = (epi == kEpiGateUp || epi == kEpiQKV);
@@ -526,7 +544,7 @@ GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const Laun
   p.n_slots = ns;
   p.smem = (size_t)ns * p.stage_bytes + (size_t)p.red_floats * 4 + 32 * 4 + (size_t)ns * 2 * 8;
   if (tp_in && !norm) return p;
-  p.fn = pick(p.kpt, p.rt, epi, tp_in ? 2 : norm ? 1 : 0);
+  p.fn = pick(p.kpt, p.rt, epi, tp_in ? 2 : norm ? 1 : 0, esz == 1 ? 1 : 0);
   p.norm = norm;
   p.ok = p.fn != nullptr && p.smem <= 226 * 1024;
   return p;

@@ -37,10 +37,11 @@ struct GemvPlan {
   bool norm;  // the kernel RMS-normalises x (GemvArgs::norm_w must then be set)
 };
 
-int gemv_kpt_for(int cols);
+int gemv_kpt_for(int cols, int esz = 2);  // esz: weight bytes (2 fp16, 1 fp8 E5M2)
 // tp_in: the kernel also adds the tensor-parallel partial sums of the previous row-parallel matvec
 // to its (normalised) input (GemvArgs::tp_ll).
-GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune, bool tp_in = false);
+GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune, bool tp_in = false,
+                   int esz = 2);
 cudaError_t gemv_prepare(const GemvPlan& p);  // once per plan, outside stream capture
 cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages);
 

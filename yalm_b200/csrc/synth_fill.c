@@ -64,6 +64,34 @@ void synth_fill_normal_f16(uint16_t* out, int64_t n, uint64_t seed, uint64_t str
   }
 }
 
+/* Writes n fp8 E5M2 values: each is the fp16 value synth_fill_normal_f16 would write for the same
+ * (seed, stream, element), rounded to nearest even on its top byte (an E5M2 value is the top byte
+ * of the fp16 with the same value). */
+void synth_fill_normal_e5m2(uint8_t* out, int64_t n, uint64_t seed, uint64_t stream, float std) {
+  const uint64_t key = splitmix64(seed * 0x2545f4914f6cdd1dull ^ splitmix64(stream + 0x632be59bd9b4e019ull));
+  const int64_t pairs = (n + 1) / 2;
+  int64_t p;
+#pragma omp parallel for schedule(static)
+  for (p = 0; p < pairs; ++p) {
+    uint64_t r = splitmix64(key + (uint64_t)p);
+    double u1 = ((double)(uint32_t)(r >> 32) + 1.0) * (1.0 / 4294967296.0);
+    double u2 = (double)(uint32_t)r * (1.0 / 4294967296.0);
+    double rad = sqrt(-2.0 * log(u1));
+    double ang = 6.283185307179586 * u2;
+    uint16_t h[2] = {f32_to_f16_rne((float)(rad * cos(ang)) * std), f32_to_f16_rne((float)(rad * sin(ang)) * std)};
+    for (int j = 0; j < 2; ++j) {
+      if (2 * p + j >= n) break;
+      uint32_t lo = h[j] & 0xFFu, up = h[j] >> 8;
+      if ((h[j] & 0x7FFFu) > 0x7C00u) {
+        up |= 0x02u; /* NaN stays NaN */
+      } else if (lo > 0x80u || (lo == 0x80u && (up & 1u))) {
+        up += 1u;
+      }
+      out[2 * p + j] = (uint8_t)up;
+    }
+  }
+}
+
 /* Writes n fp32 copies of value (norm weights). */
 void synth_fill_const_f32(float* out, int64_t n, float value) {
   int64_t i;

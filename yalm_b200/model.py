@@ -80,25 +80,34 @@ class Config:
             c.weight_dtype = "F16"
         elif dt == "fp32":
             c.weight_dtype = "F32"
+        elif dt == "fp8":
+            # convert.py's fp8 is a plain cast to float8_e5m2 (convert.py:160); yalm's runtime stops
+            # here (src/model.cpp:61-70), this engine runs it
+            c.weight_dtype = "F8_E5M2"
         else:
             raise ValueError(f"unsupported dtype: {dt}")
         return c
+
+    @property
+    def weight_bytes(self) -> int:
+        return {"F16": 2, "F32": 4, "F8_E5M2": 1}[self.weight_dtype]
 
     def to_c(self) -> _lib.yb_config:
         return _lib.yb_config(dim=self.dim, hidden_dim=self.hidden_dim, head_dim=self.head_dim,
                               n_layers=self.n_layers, n_heads=self.n_heads, n_kv_heads=self.n_kv_heads,
                               vocab_size=self.vocab_size, max_seq_len=self.max_seq_len, rotary_dim=self.rotary_dim,
                               act=int(self.act), n_experts=self.n_experts,
-                              weight_dtype=1 if self.weight_dtype == "F16" else 0,
+                              weight_dtype={"F16": 1, "F8_E5M2": 3}.get(self.weight_dtype, 0),
                               rope_theta=self.rope_theta, norm_eps=self.norm_eps, qkv_clip=self.qkv_clip)
 
     def weight_bytes_per_token(self, tp_size: int = 1) -> int:
         """Algorithmic bytes streamed per decode step on one rank: every matrix once, norms, one
         embedding row and the classifier (not the whole embedding table)."""
         q_dim, kv_dim = self.n_heads * self.head_dim, self.n_kv_heads * self.head_dim
-        per_layer = 2 * (q_dim * self.dim + 2 * kv_dim * self.dim + self.dim * q_dim
-                         + 3 * self.dim * self.hidden_dim) // tp_size + 2 * self.dim * 4
-        return self.n_layers * per_layer + 2 * self.vocab_size * self.dim // tp_size + self.dim * 4 + self.dim * 2
+        wb = self.weight_bytes
+        per_layer = wb * (q_dim * self.dim + 2 * kv_dim * self.dim + self.dim * q_dim
+                          + 3 * self.dim * self.hidden_dim) // tp_size + 2 * self.dim * 4
+        return self.n_layers * per_layer + wb * self.vocab_size * self.dim // tp_size + self.dim * 4 + self.dim * wb
 
     def kv_bytes_per_token(self, kv_len: int, tp_size: int = 1) -> int:
         """KV-cache bytes attention reads per step (K and V, fp16, all layers)."""

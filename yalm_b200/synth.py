@@ -35,6 +35,7 @@ class ModelShape:
     norm_eps: float = 1e-05
     act_type: str = "silu"
     arch: str = "MistralForCausalLM"
+    dtype: str = "fp16"  # metadata dtype: "fp16", or "fp8" (matrices as F8_E5M2, convert.py:160)
 
     @property
     def q_dim(self) -> int:
@@ -67,7 +68,7 @@ def metadata(shape: ModelShape) -> dict:
     """String-valued metadata exactly as convert.py's Metadata.to_dict (convert.py:58-81)."""
     return {
         "arch": shape.arch,
-        "dtype": "fp16",
+        "dtype": shape.dtype,
         "dim": str(shape.dim),
         "hidden_dim": str(shape.hidden_dim),
         "head_dim": str(shape.head_dim),
@@ -89,21 +90,22 @@ def metadata(shape: ModelShape) -> dict:
 def tensor_specs(shape: ModelShape):
     """(name, dtype, shape) in file order, names as convert.py writes them (convert.py:164-204)."""
     s = shape
-    out = [("model.embed.weight", "F16", (s.vocab_size, s.dim))]
+    W = "F8_E5M2" if s.dtype == "fp8" else "F16"
+    out = [("model.embed.weight", W, (s.vocab_size, s.dim))]
     for l in range(s.n_layers):
         p = f"model.layers.{l}."
         out += [
             (p + "attn.norm.weight", "F32", (s.dim,)),
-            (p + "attn.wq.weight", "F16", (s.q_dim, s.dim)),
-            (p + "attn.wk.weight", "F16", (s.kv_dim, s.dim)),
-            (p + "attn.wv.weight", "F16", (s.kv_dim, s.dim)),
-            (p + "attn.wo.weight", "F16", (s.dim, s.q_dim)),
+            (p + "attn.wq.weight", W, (s.q_dim, s.dim)),
+            (p + "attn.wk.weight", W, (s.kv_dim, s.dim)),
+            (p + "attn.wv.weight", W, (s.kv_dim, s.dim)),
+            (p + "attn.wo.weight", W, (s.dim, s.q_dim)),
             (p + "mlp.norm.weight", "F32", (s.dim,)),
-            (p + "mlp.w1.weight", "F16", (s.hidden_dim, s.dim)),
-            (p + "mlp.w2.weight", "F16", (s.dim, s.hidden_dim)),
-            (p + "mlp.w3.weight", "F16", (s.hidden_dim, s.dim)),
+            (p + "mlp.w1.weight", W, (s.hidden_dim, s.dim)),
+            (p + "mlp.w2.weight", W, (s.dim, s.hidden_dim)),
+            (p + "mlp.w3.weight", W, (s.hidden_dim, s.dim)),
         ]
-    out += [("model.norm.weight", "F32", (s.dim,)), ("model.output.weight", "F16", (s.vocab_size, s.dim))]
+    out += [("model.norm.weight", "F32", (s.dim,)), ("model.output.weight", W, (s.vocab_size, s.dim))]
     return out
 
 
@@ -115,7 +117,7 @@ def vocab_bytes(vocab_size: int) -> bytes:
     return b"".join(t.encode() + b"\0" for t in toks)
 
 
-_DTYPE_SIZE = {"F16": 2, "F32": 4, "U8": 1}
+_DTYPE_SIZE = {"F16": 2, "F32": 4, "U8": 1, "F8_E5M2": 1}
 _lib = None
 
 
@@ -131,6 +133,8 @@ def _synth_lib():
                                                ctypes.c_uint64, ctypes.c_float]
         _lib.synth_fill_const_f32.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_float]
         _lib.synth_set_threads.argtypes = [ctypes.c_int]
+        _lib.synth_fill_normal_e5m2.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint64,
+                                                ctypes.c_uint64, ctypes.c_float]
         _lib.synth_set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
     return _lib
 
@@ -172,6 +176,8 @@ def write_yalm(path: str, shape: ModelShape, seed: int = 0, std: float = 0.02) -
         n = int(np.prod(shp))
         if dt == "F32":
             lib.synth_fill_const_f32(base + o0, n, 1.0)
+        elif dt == "F8_E5M2":
+            lib.synth_fill_normal_e5m2(base + o0, n, seed, zlib.crc32(name.encode()), std)
         else:
             lib.synth_fill_normal_f16(base + o0, n, seed, zlib.crc32(name.encode()), std)
     o0, _ = header["tokenizer.tokens"]["data_offsets"]
@@ -197,3 +203,53 @@ def scratch_dir(nbytes: int) -> str:
 
 def file_bytes(shape: ModelShape) -> int:
     return sum(int(np.prod(s)) * _DTYPE_SIZE[d] for _, d, s in tensor_specs(shape)) + len(vocab_bytes(shape.vocab_size))
+
+
+def e5m2_from_f16_bits(h: np.ndarray) -> np.ndarray:
+    """fp16 bit patterns -> E5M2 bytes, rounding the low byte to nearest even (an E5M2 value is the
+    top byte of the fp16 with the same value; torch's float8_e5m2 cast of an fp16-exact value gives
+    the same bytes)."""
+    h = h.astype(np.uint32)
+    lo, up = h & 0xFF, h >> 8
+    inc = (lo > 0x80) | ((lo == 0x80) & ((up & 1) == 1))
+    nan = (h & 0x7FFF) > 0x7C00
+    out = np.where(nan, up | 0x02, up + inc.astype(np.uint32))
+    return out.astype(np.uint8)
+
+
+def expand_fp8_to_fp16(src: str, dst: str) -> str:
+    """Writes the fp16 twin of an fp8 (E5M2) .yalm file: same metadata but dtype "fp16", every
+    F8_E5M2 tensor as F16 with the identical values (byte << 8).  yalm's own fp16 CPU path on the
+    twin computes exactly what an fp8 runtime computes on the original, so it is the oracle for it."""
+    with open(src, "rb") as f:
+        n = int.from_bytes(f.read(8), "little")
+        header = json.loads(f.read(n))
+    data = np.memmap(src, dtype=np.uint8, mode="r", offset=8 + n)
+    meta = dict(header["__metadata__"], dtype="fp16")
+    names = [k for k in header if k != "__metadata__"]
+    names.sort(key=lambda k: header[k]["data_offsets"][0])
+    out_header = {"__metadata__": meta}
+    chunks = []
+    off = 0
+    for k in names:
+        e = header[k]
+        a0, a1 = e["data_offsets"]
+        raw = np.asarray(data[a0:a1])
+        if e["dtype"] == "F8_E5M2":
+            raw = (raw.astype(np.uint16) << 8).view(np.uint8)
+            dt = "F16"
+        else:
+            dt = e["dtype"]
+        out_header[k] = {"dtype": dt, "shape": e["shape"], "data_offsets": [off, off + raw.size]}
+        chunks.append(raw)
+        off += raw.size
+    hjson = json.dumps(out_header, separators=(",", ":")).encode()
+    hjson += b" " * ((-(8 + len(hjson))) % 256)
+    tmp = dst + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(len(hjson).to_bytes(8, "little"))
+        f.write(hjson)
+        for c in chunks:
+            f.write(c.tobytes())
+    os.replace(tmp, dst)
+    return dst
