@@ -255,3 +255,26 @@ extern "C" int yb_ffn(float* xout, const float* x, const uint16_t* w1, const uin
   YB_CK(cudaMemcpy(xout, dy.p, D * 4, cudaMemcpyDeviceToHost));
   return 0;
 }
+
+// ------------------------------------------------------------------------ prefill GEMM (test hook)
+#include "prefill_gemm.cuh"
+
+extern "C" int yb_prefill_gemm_dev(float* out_f32, uint16_t* out_f16, const uint16_t* a, const uint16_t* b, int M,
+                                   int N, int K, int epi, int ldo, void* stream) {
+  using namespace yb;
+  if (epi < kPreStore || epi > kPreStoreF16) return set_error(YB_E_INVALID, "bad epilogue");
+  PrefillGemmArgs g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = epi;
+  g.ldo = ldo;
+  g.out_f32 = out_f32;
+  g.out_f16 = reinterpret_cast<__half*>(out_f16);
+  g.status = nullptr;
+  cudaError_t e = prefill_gemm(reinterpret_cast<const __half*>(a), reinterpret_cast<const __half*>(b), g,
+                               static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue) return set_error(YB_E_INVALID, "unsupported GEMM shape or pointers (K % 64, N % 8, 16-byte alignment)");
+  YB_CK(e);
+  return 0;
+}

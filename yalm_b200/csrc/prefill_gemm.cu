@@ -1,0 +1,272 @@
+// Tensor-core GEMM for batched prefill on sm_100a: TMA (128-byte swizzle) into a shared-memory
+// ring, tcgen05.mma (kind::f16, M 128, N 256, K 16) accumulating in tensor memory, tcgen05.ld for
+// the fused epilogue.  One output tile of 128 tokens x 256 features per CTA.
+//
+//   warp 0      TMA producer: one elected lane fills stage s with the A and B tiles of k-block kb
+//   warp 1      owns the tensor-memory allocation; one elected lane issues the MMAs of each stage
+//               and commits them to the stage's `empty` barrier, and after the last k-block to
+//               `acc_full`
+//   warps 2-5   epilogue: each reads the 32 tensor-memory lanes (= tile rows) of its quadrant
+//               (warp % 4), 32 columns at a time, and writes the fused result
+//
+// Operand layouts follow the canonical K-major SWIZZLE_128B form of the UMMA shared-memory
+// descriptor (rows of 128 bytes, 8-row groups 1024 bytes apart); the descriptor fields are laid
+// out as the PTX ISA and CUTLASS (cute/arch/mma_sm100_desc.hpp) define them.  Every wait is
+// bounded; a wait that runs out sets the status word and the CTA stops issuing work.
+#include "prefill_gemm.cuh"
+
+#include "common.cuh"
+
+namespace yb {
+
+namespace {
+
+constexpr int kTileABytes = kPreBM * kPreBK * 2;  // 16 KB
+constexpr int kTileBBytes = kPreBN * kPreBK * 2;  // 32 KB
+constexpr int kStageBytes = kTileABytes + kTileBBytes;
+constexpr int kTmemCols = kPreBN;                 // fp32 accumulator: 128 lanes x 256 columns
+
+// 2-D TMA tile load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor, K-major, SWIZZLE_128B: start address, leading byte offset 16 (unused
+// for swizzled K-major), stride byte offset 1024 (8 rows of 128 bytes), version 1, layout 2.
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// Instruction descriptor: fp16 A and B, fp32 accumulator, both K-major, M 128, N 256.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kPreBN >> 3) << 17) | ((uint32_t)(kPreBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_c, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+      ::"r"(tmem_c), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every MMA this thread issued before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kPreThreads, 1)
+    prefill_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const PrefillGemmArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // stage buffers must start on a 1024-byte boundary (swizzle atom)
+  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full[kPreStages], empty[kPreStages], acc_full;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kPreBM, n0 = blockIdx.x * kPreBN;
+  const int nk = a.K / kPreBK;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < kPreStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    // whole warp: allocate the accumulator columns, publish the address
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(&s_tmem)), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      int issued = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kPreStages;
+        if (kb >= kPreStages && !mbar_wait(&empty[s], ((kb / kPreStages) - 1) & 1, a.status)) {
+          s_abort = 1;
+          break;
+        }
+        unsigned char* sa = smem + (size_t)s * kStageBytes;
+        mbar_arrive_expect_tx(&full[s], (unsigned)kStageBytes);
+        tma_load_2d(sa, &map_a, kb * kPreBK, m0, &full[s]);
+        tma_load_2d(sa + kTileABytes, &map_b, kb * kPreBK, n0, &full[s]);
+        issued = kb + 1;
+      }
+      // never leave while a tile load issued here may still be landing: the last armed phase of
+      // each stage must have completed (already true unless a wait gave up)
+      for (int kb = max(0, issued - kPreStages); kb < issued; ++kb)
+        mbar_wait(&full[kb % kPreStages], (kb / kPreStages) & 1, a.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kPreStages;
+        if (!mbar_wait(&full[s], (kb / kPreStages) & 1, a.status)) {
+          ok = false;
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + (size_t)s * kStageBytes);
+        const uint32_t sb = sa + kTileABytes;
+#pragma unroll
+        for (int k = 0; k < kPreBK / 16; ++k)  // 16 fp16 = 32 bytes further along the swizzled row
+          umma_f16(tmem, umma_desc_k_sw128(sa + k * 32), umma_desc_k_sw128(sb + k * 32), (kb | k) ? 1u : 0u);
+        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      if (ok) umma_commit(&acc_full);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (warps 2-5)
+    const int quad = warp & 3;  // tensor-memory lanes [32 quad, 32 quad + 32) = tile rows
+    const bool ready = mbar_wait(&acc_full, 0, a.status);
+    tc_fence_after();
+    const int row = m0 + quad * 32 + lane;
+    if (ready && !*(volatile int*)&s_abort) {
+      for (int c0 = 0; c0 < kPreBN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, v);
+        if (row >= a.M) continue;
+        const int col = n0 + c0;
+        if (a.epi == kPreSwiGLU) {
+          // (gate, up) column pairs -> silu(gate) * up at column col / 2 + i
+          __half* o = a.out_f16 + (size_t)row * a.ldo + col / 2;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (col + 2 * i + 1 < a.N) {
+              const float g = v[2 * i], u = v[2 * i + 1];
+              o[i] = __float2half_rn(g / (1.0f + expf(-g)) * u);
+            }
+          }
+        } else if (a.epi == kPreStoreF16) {
+          __half* o = a.out_f16 + (size_t)row * a.ldo + col;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (col + i < a.N) o[i] = __float2half_rn(v[i]);
+        } else {
+          float* o = a.out_f32 + (size_t)row * a.ldo + col;
+          if (col + 32 <= a.N) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 r = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+              if (a.epi == kPreAdd) {
+                const float4 p = *reinterpret_cast<const float4*>(o + i);
+                r.x += p.x; r.y += p.y; r.z += p.z; r.w += p.w;
+              }
+              *reinterpret_cast<float4*>(o + i) = r;
+            }
+          } else {
+            for (int i = 0; i < 32 && col + i < a.N; ++i) o[i] = a.epi == kPreAdd ? o[i] + v[i] : v[i];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------------- host side
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Row-major fp16 matrix [rows][cols] read in boxes of box_rows x 64 columns, 128-byte swizzle;
+// rows beyond the matrix read as zeros.
+bool make_map(CUtensorMap* m, const __half* base, int rows, int cols, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kPreBK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t prefill_gemm(const __half* A, const __half* B, const PrefillGemmArgs& args, cudaStream_t stream) {
+  if (args.M <= 0 || args.N <= 0 || args.K <= 0 || args.K % kPreBK || args.N % 8 ||
+      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
+    return cudaErrorInvalidValue;
+  if ((args.epi == kPreSwiGLU || args.epi == kPreStoreF16) ? !args.out_f16 : !args.out_f32) return cudaErrorInvalidValue;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, A, args.M, args.K, kPreBM) || !make_map(&mb, B, args.N, args.K, kPreBN))
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)kPreStages * kStageBytes + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const dim3 grid((args.N + kPreBN - 1) / kPreBN, (args.M + kPreBM - 1) / kPreBM);
+  prefill_gemm_kernel<<<grid, kPreThreads, smem, stream>>>(ma, mb, args);
+  return cudaGetLastError();
+}
+
+}  // namespace yb
