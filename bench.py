@@ -251,9 +251,10 @@ def main():
     prompt = rng.integers(0, c.vocab_size, PROMPT_LEN)
     stream_toks = rng.integers(0, c.vocab_size, 4096)
     s = InferenceState(c)
-    for pos, tok in enumerate(prompt[:-1]):
-        m.forward_async(int(tok), pos, InferenceMode.HYDRATE_KV_CACHE)
-    m.forward(s, int(prompt[-1]), PROMPT_LEN - 1, InferenceMode.OUTPUT_LOGITS)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    m.prefill([int(t) for t in prompt], 0, s)  # batched when the engine supports it, else per token
+    t_prompt = time.perf_counter() - t0
 
     def pos_of(i):
         return PROMPT_LEN + (i % DECODE_LEN)
@@ -431,6 +432,8 @@ def main():
             "step_roofline": {"bytes_per_step_per_rank": step_bytes, "achieved_gbs": round(step_gbs, 1), "peak": peak,
                               "frac": round(step_gbs / peak, 4)},
             "executor": executor,
+            "prompt": {"tokens": PROMPT_LEN, "seconds": round(t_prompt, 4),
+                       "tok_s": round(PROMPT_LEN / max(t_prompt, 1e-9), 1), "api": "yb_prefill"},
             "engine_load": {"seconds": round(t_load, 2), "weight_bytes_per_rank": c.weight_bytes_per_token(world),
                             "gb_s": round(c.weight_bytes_per_token(world) / max(t_load, 1e-9) / 1e9, 1),
                             "source": "checkpoint pages in the host page cache (tmpfs)"},
@@ -462,11 +465,19 @@ def long_context(m, c, args, stream, world, dist, peak):
     prompt = rng.integers(0, c.vocab_size, LONG_PREFILL)
     toks = rng.integers(0, c.vocab_size, LONG_DECODE)
     torch.cuda.synchronize()
+    # yalm's prompt loop, one token per step (src/main.cpp:171-177)
     t0 = time.perf_counter()
     for pos, tok in enumerate(prompt):
         m.forward_async(int(tok), pos, InferenceMode.HYDRATE_KV_CACHE if pos + 1 < LONG_PREFILL else InferenceMode.OUTPUT_LOGITS)
     m.sync()
     t_prefill = time.perf_counter() - t0
+    # the same prompt in one batched pass (yb_prefill: tensor-core GEMMs), which leaves the cache the
+    # decode steps below read
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    m.prefill(prompt, 0)
+    t_batched = time.perf_counter() - t0
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -488,6 +499,8 @@ def long_context(m, c, args, stream, world, dist, peak):
                        f"kv_len {LONG_PREFILL + 1}..{LONG_PREFILL + LONG_DECODE}",
            "decode_tok_s": round(LONG_DECODE / (ms / 1000.0), 3), "ms_per_step": round(ms / LONG_DECODE, 4),
            "prefill_tok_s_one_token_steps": round(LONG_PREFILL / t_prefill, 1),
+           "prefill_tok_s_batched": round(LONG_PREFILL / t_batched, 1),
+           "prefill_batched_s": round(t_batched, 4),
            "step_roofline": {"bytes_per_step_per_rank": step_bytes,
                              "achieved_gbs": round(step_bytes / (ms / LONG_DECODE / 1000.0) / 1e9, 1),
                              "frac": round(step_bytes / (ms / LONG_DECODE / 1000.0) / 1e9 / peak, 4)}}

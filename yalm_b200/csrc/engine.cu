@@ -827,6 +827,9 @@ extern "C" void yb_destroy(yb_engine* e) {
   if (e->tp.d_peer_counters) cudaFree(e->tp.d_peer_counters);
   if (e->tp.base) cudaFree(e->tp.base);
   for (void* p : e->allocs) cudaFree(p);
+  for (void* v : {(void*)e->pf.x, (void*)e->pf.xn, (void*)e->pf.qkv, (void*)e->pf.q, (void*)e->pf.att, (void*)e->pf.h,
+                  (void*)e->pf.tokens})
+    if (v) cudaFree(v);
   if (e->status_h) cudaFreeHost(e->status_h);
   if (e->sample_h) cudaFreeHost(e->sample_h);
   if (e->stream) cudaStreamDestroy(e->stream);

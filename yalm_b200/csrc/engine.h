@@ -134,6 +134,17 @@ struct yb_engine {
   unsigned epoch = 0;
   unsigned lepoch = 0;
   yb::TpRegion tp;
+  // batched prefill work buffers (allocated on first use, grown to the largest prompt)
+  struct Prefill {
+    int cap = 0;
+    float* x = nullptr;       // [cap][dim] residual stream
+    __half* xn = nullptr;     // [cap][dim] normalised, fp16 GEMM operand
+    float* qkv = nullptr;     // [cap][q + 2 kv]
+    float* q = nullptr;       // [cap][q_rows] after RoPE
+    __half* att = nullptr;    // [cap][q_rows]
+    __half* h = nullptr;      // [cap][hidden_l]
+    int* tokens = nullptr;    // [cap]
+  } pf;
 };
 
 namespace yb {

@@ -258,11 +258,13 @@ cudaError_t prefill_gemm(const __half* A, const __half* B, const PrefillGemmArgs
   if (!make_map(&ma, A, args.M, args.K, kPreBM) || !make_map(&mb, B, args.N, args.K, kPreBN))
     return cudaErrorInvalidValue;
   const size_t smem = (size_t)kPreStages * kStageBytes + 1024;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static bool attr_set[64] = {};  // per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const dim3 grid((args.N + kPreBN - 1) / kPreBN, (args.M + kPreBM - 1) / kPreBM);
   prefill_gemm_kernel<<<grid, kPreThreads, smem, stream>>>(ma, mb, args);

@@ -1,0 +1,122 @@
+// yb_prefill: a prompt through the model in one batched pass (tensor-core GEMMs for every matrix,
+// causal attention over the new and the cached slots), replacing the token-by-token prompt loop of
+// yalm's run_completion (src/main.cpp:171-177).  The KV cache ends up as the per-token steps would
+// leave it (to fp16 rounding of the activations); the last token's logits come from the decode
+// classifier kernel.
+#include "engine.h"
+#include "prefill.cuh"
+#include "prefill_gemm.cuh"
+
+#include <algorithm>
+#include <cstring>
+
+using namespace yb;
+
+namespace {
+
+__global__ void prefill_embed_kernel(const __half* emb, const int* tokens, float* x, int dim) {
+  const __half* row = emb + (size_t)tokens[blockIdx.x] * dim;
+  float* xr = x + (size_t)blockIdx.x * dim;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) xr[i] = __half2float(row[i]);
+}
+
+int ensure_buffers(yb_engine* e, int T) {
+  auto& p = e->pf;
+  if (p.cap >= T) return 0;
+  const yb_config& c = e->cfg;
+  void* old[] = {p.x, p.xn, p.qkv, p.q, p.att, p.h, p.tokens};
+  for (void* v : old) if (v) cudaFree(v);
+  p = yb_engine::Prefill{};
+  const size_t cap = (size_t)((T + 127) / 128 * 128);
+  const size_t qkv_rows = (size_t)e->q_rows + 2 * e->kv_rows;
+  YB_CK(cudaMalloc(&p.x, cap * c.dim * 4));
+  YB_CK(cudaMalloc(&p.xn, cap * c.dim * 2));
+  YB_CK(cudaMalloc(&p.qkv, cap * qkv_rows * 4));
+  YB_CK(cudaMalloc(&p.q, cap * e->q_rows * 4));
+  YB_CK(cudaMalloc(&p.att, cap * e->q_rows * 2));
+  YB_CK(cudaMalloc(&p.h, cap * e->hid * 2));
+  YB_CK(cudaMalloc(&p.tokens, cap * 4));
+  p.cap = (int)cap;
+  return 0;
+}
+
+int gemm(const __half* A, const __half* B, int M, int N, int K, int epi, float* of, __half* oh, int ldo,
+         cudaStream_t s) {
+  PrefillGemmArgs g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epi = epi;
+  g.ldo = ldo;
+  g.out_f32 = of;
+  g.out_f16 = oh;
+  g.status = nullptr;
+  YB_CK(prefill_gemm(A, B, g, s));
+  return 0;
+}
+
+}  // namespace
+
+// Whether the batched path covers this engine and prompt (else the per-token steps run).
+static bool batched_ok(const yb_engine* e, int n, int pos0) {
+  const yb_config& c = e->cfg;
+  return e->tp_size == 1 && e->esz == 2 && c.act == 1 && n >= 2 && pos0 + n <= c.max_seq_len &&
+         c.dim % 64 == 0 && e->q_rows % 64 == 0 && e->hid % 64 == 0 && (c.head_dim == 64 || c.head_dim == 128);
+}
+
+extern "C" int yb_prefill(yb_engine* e, const int* tokens, int n, int pos0, float* logits) {
+  if (!e || !tokens || n <= 0 || pos0 < 0) return set_error(YB_E_INVALID, "bad prefill arguments");
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= e->cfg.vocab_size) return set_error(YB_E_INVALID, "token out of range");
+  if (!batched_ok(e, n, pos0)) {
+    // per-token steps, as yalm's prompt loop runs them
+    for (int i = 0; i < n; ++i) {
+      const bool last = i + 1 == n;
+      int rc = yb_forward(e, tokens[i], pos0 + i, last && logits ? YB_MODE_OUTPUT_LOGITS : YB_MODE_HYDRATE_KV_CACHE,
+                          last ? logits : nullptr);
+      if (rc) return rc;
+    }
+    return yb_sync(e);
+  }
+  YB_CK(cudaSetDevice(e->device));
+  int rc = ensure_buffers(e, n);
+  if (rc) return rc;
+  const yb_config& c = e->cfg;
+  cudaStream_t s = e->stream;
+  auto& p = e->pf;
+  const int qkv_rows = e->q_rows + 2 * e->kv_rows;
+  YB_CK(cudaMemcpyAsync(p.tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  prefill_embed_kernel<<<n, 256, 0, s>>>(e->emb, p.tokens, p.x, c.dim);
+  YB_CK(cudaGetLastError());
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerBuffers& L = e->layers[l];
+    YB_CK(prefill_rmsnorm(p.x, L.rms_att, p.xn, n, c.dim, c.norm_eps, s));
+    if ((rc = gemm(p.xn, L.wqkv, n, qkv_rows, c.dim, kPreStore, p.qkv, nullptr, qkv_rows, s))) return rc;
+    YB_CK(prefill_qkv_post(p.qkv, n, pos0, e->q_rows, e->kv_rows, c.head_dim, c.rotary_dim, c.max_seq_len, c.qkv_clip,
+                           e->inv_freq, p.q, L.k_cache, L.v_cache, s));
+    YB_CK(prefill_attention(p.q, L.k_cache, L.v_cache, p.att, n, pos0, e->nh, e->nkv, c.head_dim, c.max_seq_len, s));
+    if ((rc = gemm(p.att, L.wo, n, c.dim, e->q_rows, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
+    YB_CK(prefill_rmsnorm(p.x, L.rms_ffn, p.xn, n, c.dim, c.norm_eps, s));
+    if ((rc = gemm(p.xn, L.w13, n, 2 * e->hid, c.dim, kPreSwiGLU, nullptr, p.h, e->hid, s))) return rc;
+    if ((rc = gemm(p.h, L.w2, n, c.dim, e->hid, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
+  }
+  // the last token's residual stream -> the decode classifier (final RMSNorm + logits)
+  YB_CK(cudaMemcpyAsync(e->x, p.x + (size_t)(n - 1) * c.dim, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
+  if (logits) {
+    GemvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.status = e->status_d;
+    a.eps = c.norm_eps;
+    a.tp_size = 1;
+    a.w = e->wcls;
+    a.ldw = c.dim;
+    a.rows = e->vocab_l;
+    a.cols = c.dim;
+    a.x = e->x;
+    a.norm_w = e->rms_final;
+    a.y = e->logits;
+    YB_CK(gemv_launch(e->plan_cls, a, s, false, 0));
+    YB_CK(cudaMemcpyAsync(logits, e->logits, (size_t)c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
+  }
+  return yb_sync(e);
+}

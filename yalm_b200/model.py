@@ -230,6 +230,15 @@ class Model:
     def forward_async(self, token: int, pos: int, mode: InferenceMode = InferenceMode.OUTPUT_LOGITS) -> None:
         _lib.call("yb_forward_async", self.engine, int(token), int(pos), int(mode))
 
+    def prefill(self, tokens, pos0: int = 0, s: InferenceState | None = None) -> None:
+        """The prompt loop of yalm's run_completion (src/main.cpp:171-177) in one batched pass:
+        tokens at positions pos0.., KV cache filled; with `s` the last token's logits land in
+        s.logits()."""
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        lg = s.logits() if s is not None else None
+        _lib.call("yb_prefill", self.engine, ids.ctypes.data, int(ids.size), int(pos0),
+                  lg.ctypes.data if lg is not None else None)
+
     def forward_sample(self, token: int, pos: int, temperature: float = 0.0, coin: float = 0.0) -> int:
         """Model::forward + Sampler::sample (src/sampler.cpp:27-64) with the sampler on the device:
         returns the next token id; temperature 0 is greedy, else `coin` plays yalm's
