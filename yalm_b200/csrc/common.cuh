@@ -206,45 +206,59 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
   return v[0];
 }
 
+// Packed fp32 pair arithmetic (sm_100): two IEEE fp32 operations per instruction, each rounded
+// exactly as the scalar fmaf / multiply would be.
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+  unsigned long long u;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(u) : "f"(v.x), "f"(v.y));
+  return u;
+}
+__device__ __forceinline__ float2 bits_f2(unsigned long long u) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(u));
+  return v;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+
 // 16 fp8 E5M2 weights (one 16-byte vector) dotted with 16 fp32 activations.  An E5M2 value is
 // the top byte of the fp16 with the same value, so a byte permute that puts each byte above a zero
-// byte yields two fp16 values per 32-bit word, exactly; two FMA chains as in dot8.
+// byte yields two fp16 values per 32-bit word, exactly; even and odd elements accumulate in the two
+// halves of a packed fp32 pair (two FMA chains, as in dot8).
 __device__ __forceinline__ float dot16_e5m2(uint4 w, const float4& x0, const float4& x1, const float4& x2,
                                             const float4& x3) {
   const unsigned q[4] = {w.x, w.y, w.z, w.w};
   const float4* xs[4] = {&x0, &x1, &x2, &x3};
-  float a0 = 0.f, a1 = 0.f;
+  float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const unsigned lo = __byte_perm(q[i], 0u, 0x1404u);  // elements 4i, 4i+1 as fp16
     const unsigned hi = __byte_perm(q[i], 0u, 0x3424u);  // elements 4i+2, 4i+3
     const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&lo));
     const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&hi));
-    a0 = fmaf(f0.x, xs[i]->x, a0);
-    a1 = fmaf(f0.y, xs[i]->y, a1);
-    a0 = fmaf(f1.x, xs[i]->z, a0);
-    a1 = fmaf(f1.y, xs[i]->w, a1);
+    acc = fma2(f0, make_float2(xs[i]->x, xs[i]->y), acc);
+    acc = fma2(f1, make_float2(xs[i]->z, xs[i]->w), acc);
   }
-  return a0 + a1;
+  return acc.x + acc.y;
 }
 
-// 8 fp16 weights (one 16-byte vector) dotted with 8 fp32 activations: two independent 4-long FMA
-// chains (even / odd elements), so the dependency chain is half as long.
+// 8 fp16 weights (one 16-byte vector) dotted with 8 fp32 activations: even and odd elements in the
+// two halves of a packed fp32 pair (two independent 4-long FMA chains, half the FMA instructions).
 __device__ __forceinline__ float dot8(uint4 w, const float4& xa, const float4& xb) {
   const __half2* h = reinterpret_cast<const __half2*>(&w);
-  const float2 f0 = __half22float2(h[0]);
-  const float2 f1 = __half22float2(h[1]);
-  const float2 f2 = __half22float2(h[2]);
-  const float2 f3 = __half22float2(h[3]);
-  float e = f0.x * xa.x;
-  float o = f0.y * xa.y;
-  e = fmaf(f1.x, xa.z, e);
-  o = fmaf(f1.y, xa.w, o);
-  e = fmaf(f2.x, xb.x, e);
-  o = fmaf(f2.y, xb.y, o);
-  e = fmaf(f3.x, xb.z, e);
-  o = fmaf(f3.y, xb.w, o);
-  return e + o;
+  float2 acc = mul2(__half22float2(h[0]), make_float2(xa.x, xa.y));
+  acc = fma2(__half22float2(h[1]), make_float2(xa.z, xa.w), acc);
+  acc = fma2(__half22float2(h[2]), make_float2(xb.x, xb.y), acc);
+  acc = fma2(__half22float2(h[3]), make_float2(xb.z, xb.w), acc);
+  return acc.x + acc.y;
 }
 
 __device__ __forceinline__ uint4 lds128(const void* p) {
