@@ -149,8 +149,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   bool ok = true;
   // Scores of every staged slot (both sub-chunks) first, then one softmax over the slice and one
   // pass over V: the slice is at most 128 slots, so no running rescale is needed.
+  // The sub-chunk loops stay rolled: this code runs once per CTA, so its instruction fetches miss
+  // the instruction cache; a smaller body is faster than an unrolled one here.
   float sc[SLOTS][ROUNDS];
-#pragma unroll
+#pragma unroll 1
   for (int j = 0; j < SLOTS; ++j) {
 #pragma unroll
     for (int r = 0; r < ROUNDS; ++r) sc[j][r] = -INFINITY;
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
       if (j < n_sub) mx = fmaxf(mx, fmaxf(S[(j * GQ + h) * kAttnSub + lane], S[(j * GQ + h) * kAttnSub + lane + 32]));
     m_run[h] = warp_max(mx);
   }
-#pragma unroll
+#pragma unroll 1
   for (int j = 0; j < SLOTS; ++j) {
     if (j >= n_sub) break;
     const __half* Vj = Vs + (size_t)j * kAttnSub * HD;
