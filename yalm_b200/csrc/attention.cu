@@ -47,12 +47,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 0);
 
   const int s_max = gridDim.x;
-  // Slices of at least one staged sub-chunk (short contexts need no merge at all); slice sidx of a
-  // cache of len slots covers [t0, t1) in n_sub sub-chunks (0 = inactive).
+  // A cache of at most one CTA's capacity goes to slice 0 alone (no merge); longer ones split into
+  // slices of at least one staged sub-chunk. Slice sidx of a cache of len slots covers [t0, t1) in
+  // n_sub sub-chunks (0 = inactive).
   auto partition = [&](int len, int& t0_, int& t1_, int& nsub_, int& nact_) {
     int ch = (len + s_max - 1) / s_max;
     ch = ((ch + 15) / 16) * 16;
-    if (ch < kAttnSub) ch = kAttnSub;
+    if (len <= kAttnCapacity) ch = kAttnCapacity;
+    else if (ch < kAttnSub) ch = kAttnSub;
     nact_ = (len + ch - 1) / ch;
     t0_ = sidx * ch;
     t1_ = min(len, t0_ + ch);
