@@ -27,7 +27,8 @@ NVCC_FLAGS = ARCH + [
     "-Xcompiler", "-fPIC,-O3", "-I" + os.path.join(ROOT, "include"),
 ]
 CU_SOURCES = ["gemv.cu", "attention.cu", "persistent.cu", "engine.cu", "capi.cu", "noalloc.cu", "sampler.cu", "loader.cu", "prefill_gemm.cu", "prefill.cu", "prefill_run.cu"]
-HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "persistent.cuh", "launch.h", "engine.h"]
+HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "persistent.cuh", "launch.h", "engine.h", "loader.h", "prefill.cuh",
+           "prefill_gemm.cuh", "sampler.cuh", "tmap.h"]
 
 
 def _newer(target: str, deps) -> bool:

@@ -7,6 +7,7 @@
 //    code in a status word the host reads after each step, and lets the kernel return.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -32,43 +33,56 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ---------------------------------------------------------------- mbarrier
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+// The *_s forms take 32-bit shared-window addresses; the pointer forms convert with smem_u32, which
+// must only see pointers derived from a __shared__ object by pointer arithmetic (a pointer rebuilt
+// from an integer has no shared provenance, and its conversion is undefined).
+__device__ __forceinline__ void mbar_init_s(uint32_t bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) { mbar_init_s(smem_u32(bar), count); }
 // Makes barrier initialisation visible to the async (TMA) proxy before the first bulk copy.
 __device__ __forceinline__ void mbar_fence_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+__device__ __forceinline__ void mbar_arrive_expect_tx_s(uint32_t bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+  mbar_arrive_expect_tx_s(smem_u32(bar), bytes);
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+__device__ __forceinline__ bool mbar_try_wait_s(uint32_t bar, unsigned parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  return mbar_try_wait_s(smem_u32(bar), parity);
+}
 // Waits for the barrier phase with the given parity.  Returns false (and records kStatusMbarTimeout)
 // when the cycle budget runs out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* status) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __forceinline__ bool mbar_wait_s(uint32_t bar, unsigned parity, unsigned* status) {
+  if (mbar_try_wait_s(bar, parity)) return true;
   long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_s(bar, parity)) {
     if (clock64() - t0 > kWaitBudgetCycles) {
       if (status) atomicOr(status, kStatusMbarTimeout);
       return false;
     }
   }
   return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* status) {
+  return mbar_wait_s(smem_u32(bar), parity, status);
 }
 
 // ---------------------------------------------------------------- bulk copies (1-D TMA)
@@ -88,16 +102,72 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, unsign
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
-__device__ __forceinline__ void bulk_g2s_nohint(void* dst_smem, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst_smem)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+__device__ __forceinline__ void bulk_g2s_nohint_s(uint32_t dst, const void* src, unsigned bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
                : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_nohint(void* dst_smem, const void* src, unsigned bytes, uint64_t* bar) {
+  bulk_g2s_nohint_s(smem_u32(dst_smem), src, bytes, smem_u32(bar));
 }
 // Fire-and-forget prefetch of a global range into L2 (bytes a multiple of 16).
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
+
+// 2-D tiled TMA load of one box of `map` at element coordinates (x inner, y outer) into shared
+// memory, completing on `bar`.  x times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d_s(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  tma_load_2d_s(smem_u32(dst), map, x, y, smem_u32(bar));
+}
+
+// ---------------------------------------------------------------- warp-level mma (m16n8k16, fp16)
+// Fragment layouts as the PTX ISA defines them for mma.m16n8k16 with .f16 inputs: with
+// g = lane / 4 and c = lane % 4, A (16 x 16, row) holds {(g, 2c..2c+1), (g+8, 2c..), (g, 2c+8..),
+// (g+8, 2c+8..)}, B (16 x 8, col) holds {(k 2c..2c+1, n g), (k 2c+8.., n g)}, C/D (16 x 8, f32)
+// holds {(g, 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)}.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr)
+               : "memory");
+}
+// Transposes the 8 x 8 fp16 matrix whose rows the warp holds in the (g, 2c..2c+1) layout.
+__device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// fp32 pair split into an fp16 pair and its fp16 remainder: x = hi + lo to about 22 bits, so a
+// product with an fp16 operand keeps nearly fp32 accuracy over two mma passes.
+__device__ __forceinline__ void split_f16x2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const __half2 l = __floats2half2_rn(x - __low2float(h), y - __high2float(h));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+// Byte offset of 16-byte chunk c (0..7) of row r in a box of 128-byte rows written by TMA with
+// CU_TENSOR_MAP_SWIZZLE_128B (box base 1024-byte aligned).
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 // ---------------------------------------------------------------- system-scope flags (peer memory)
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {

@@ -16,6 +16,7 @@
 #include "prefill_gemm.cuh"
 
 #include "common.cuh"
+#include "tmap.h"
 
 namespace yb {
 
@@ -27,12 +28,6 @@ constexpr int kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = kPreBN;                 // fp32 accumulator: 128 lanes x 256 columns
 
 // 2-D TMA tile load (no multicast) completing on an mbarrier.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // UMMA shared-memory descriptor, K-major, SWIZZLE_128B: start address, leading byte offset 16 (unused
 // for swizzled K-major), stride byte offset 1024 (8 rows of 128 bytes), version 1, layout 2.
@@ -89,7 +84,8 @@ __global__ void __launch_bounds__(kPreThreads, 1)
                         const PrefillGemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // stage buffers must start on a 1024-byte boundary (swizzle atom)
-  unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // (aligned in the shared address space; the pointer steps by the same pad and keeps its provenance)
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   __shared__ __align__(8) uint64_t full[kPreStages], empty[kPreStages], acc_full;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
@@ -217,34 +213,10 @@ __global__ void __launch_bounds__(kPreThreads, 1)
 // ---------------------------------------------------------------------------------- host side
 namespace {
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return (EncodeTiledFn) nullptr;
-    return reinterpret_cast<EncodeTiledFn>(p);
-  }();
-  return fn;
-}
-
 // Row-major fp16 matrix [rows][cols] read in boxes of box_rows x 64 columns, 128-byte swizzle;
 // rows beyond the matrix read as zeros.
 bool make_map(CUtensorMap* m, const __half* base, int rows, int cols, int box_rows) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kPreBK, (cuuint32_t)box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return tmap_f16_2d_sw128(m, base, rows, cols, kPreBK, box_rows);
 }
 
 }  // namespace
