@@ -265,6 +265,14 @@ int yb_attention_dev_noalloc(float* out, const float* q, const uint16_t* k_cache
 int yb_prefill_gemm_dev(float* out_f32, uint16_t* out_f16, const uint16_t* a, const uint16_t* b, int M, int N, int K,
                         int epi, int ldo, void* stream);
 
+/* Batched-prefill causal attention on device buffers (the per-token loop of yalm's attention,
+ * src/infer.cpp:218-250, for T new tokens at positions pos0 .. pos0 + T - 1 at once): q fp32
+ * [T][n_heads * head_dim] (after RoPE), the head-major fp16 caches [n_kv_heads][max_seq_len][head_dim]
+ * already holding slots 0 .. pos0 + T - 1; out fp16 [T][n_heads * head_dim].  Token t attends to
+ * slots 0 .. pos0 + t. */
+int yb_prefill_attention_dev(uint16_t* out, const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int T,
+                             int pos0, int n_heads, int n_kv_heads, int head_dim, int max_seq_len, void* stream);
+
 /* Number of streaming multiprocessors the kernels size their grids for (device 0 if none set). */
 int yb_num_sms(void);
 

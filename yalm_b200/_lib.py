@@ -56,6 +56,7 @@ _SIGS = {
     "yb_forward_sample": (_I, [_P, _I, _I, ctypes.c_float, ctypes.c_float, _P]),
     "yb_forward_prob": (_I, [_P, _I, _I, _I, _P]),
     "yb_prefill_gemm_dev": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "yb_prefill_attention_dev": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
     "yb_prefill": (_I, [_P, _P, _I, _I, _P]),
     "yb_forward_async": (_I, [_P, _I, _I, _I]),
     "yb_sync": (_I, [_P]),

@@ -257,7 +257,19 @@ extern "C" int yb_ffn(float* xout, const float* x, const uint16_t* w1, const uin
 }
 
 // ------------------------------------------------------------------------ prefill GEMM (test hook)
+#include "prefill.cuh"
 #include "prefill_gemm.cuh"
+
+extern "C" int yb_prefill_attention_dev(uint16_t* out, const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                        int T, int pos0, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
+                                        void* stream) {
+  using namespace yb;
+  if (!out || !q || !k_cache || !v_cache) return set_error(YB_E_INVALID, "null buffer");
+  YB_CK(prefill_attention(q, reinterpret_cast<const __half*>(k_cache), reinterpret_cast<const __half*>(v_cache),
+                          reinterpret_cast<__half*>(out), T, pos0, n_heads, n_kv_heads, head_dim, max_seq_len,
+                          static_cast<cudaStream_t>(stream)));
+  return 0;
+}
 
 extern "C" int yb_prefill_gemm_dev(float* out_f32, uint16_t* out_f16, const uint16_t* a, const uint16_t* b, int M,
                                    int N, int K, int epi, int ldo, void* stream) {

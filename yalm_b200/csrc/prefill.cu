@@ -90,13 +90,19 @@ cudaError_t prefill_qkv_post(const float* qkv, int T, int pos0, int q_rows, int 
 
 // ----------------------------------------------------------------------------- causal attention
 // CTA = (block of QB queries, kv head g); 8 warps, each owning R = 16 (query, head) rows: QW = 16 / GQ
-// queries x the GQ heads of the group.  Key tiles of 64 slots are staged in shared memory (K rows
-// padded to a 16-byte-odd stride so lanes reading different rows hit different banks); per tile a
-// warp scores its 16 rows against 2 keys per lane, updates the running max / sum (online softmax),
-// stages the probabilities and accumulates P.V with each lane owning head_dim / 32 output dims.
+// queries x the GQ heads of the group, so every K/V tile staged in shared memory serves the GQ query
+// heads of its kv head.  Per key tile of 64 slots a warp works on the tensor cores (mma.sync
+// m16n8k16, fp32 accumulate), flash-attention style:
+//   S[16 rows][64 keys] = Q . K^T     (q split into fp16 hi + lo parts: the products keep ~22 bits)
+//   causal mask, online softmax (running max / sum per row, rescaling O when the max grows)
+//   O[16 rows][HD] += P . V           (p split the same way)
+// The S accumulator fragments become the P operand fragments in registers (same row / column
+// layout).  K and V rows are staged with a padded stride (an odd multiple of 16 bytes) so the eight
+// rows one ldmatrix reads fall in different bank groups.
 namespace {
 constexpr int kPaRows = 16;
 constexpr int kPaKeys = 64;
+__host__ __device__ constexpr int pa_row_bytes(int hd) { return hd * 2 + 16; }
 }  // namespace
 
 template <int HD, int GQ>
@@ -106,15 +112,17 @@ __global__ void __launch_bounds__(256, 1)
                              int n_heads, int msl) {
   constexpr int QW = kPaRows / GQ;  // queries per warp
   constexpr int QB = 8 * QW;        // queries per CTA
-  constexpr int DPL = HD / 32;      // output dims per lane
-  constexpr int KS = HD + 8;        // padded K row (halves): 16-byte stride odd
+  constexpr int KS = HD / 16;       // k-steps of S over head_dim
+  constexpr int NT = HD / 8;        // n-tiles of O
+  constexpr int RB = pa_row_bytes(HD);
+  constexpr int CPR = HD / 8;       // 16-byte chunks per cache row
   extern __shared__ __align__(16) unsigned char smem[];
-  float* Qs = reinterpret_cast<float*>(smem);                      // [8][16][HD]
-  float* Ps = Qs + 8 * kPaRows * HD;                               // [8][16][64]
-  __half* Ks = reinterpret_cast<__half*>(Ps + 8 * kPaRows * kPaKeys);  // [64][KS]
-  __half* Vs = Ks + kPaKeys * KS;                                  // [64][HD]
+  unsigned char* Ks = smem;                  // [64][RB]
+  unsigned char* Vs = smem + kPaKeys * RB;   // [64][RB]
+  const uint32_t ks_s = smem_u32(Ks), vs_s = smem_u32(Vs);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g4 = lane >> 2, c4 = lane & 3;
   const int nqb = (T + QB - 1) / QB;
   const int qb = nqb - 1 - (int)blockIdx.x;  // longest blocks first
   const int g = blockIdx.y;
@@ -124,138 +132,158 @@ __global__ void __launch_bounds__(256, 1)
   const __half* vg = v_cache + (size_t)g * msl * HD;
   const int q_dim = n_heads * HD;
 
-  // this warp's rows: r = qi * GQ + h -> query q0 + warp * QW + qi, head g * GQ + h
-  float* Qw = Qs + (size_t)warp * kPaRows * HD;
-  for (int e = lane; e < kPaRows * HD; e += 32) {
-    const int r = e / HD, d = e % HD;
-    const int t = q0 + warp * QW + r / GQ;
-    Qw[e] = t < T ? q[(size_t)t * q_dim + (size_t)(g * GQ + r % GQ) * HD + d] : 0.f;
+  // This lane's two rows: half hf holds row g4 + 8 hf = qi * GQ + h -> query q0 + warp * QW + qi,
+  // head g * GQ + h.
+  int tq[2], qpos[2];
+  const float* qrow[2];
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    const int r = g4 + 8 * hf;
+    tq[hf] = q0 + warp * QW + r / GQ;
+    qpos[hf] = pos0 + tq[hf];
+    qrow[hf] = q + (size_t)(tq[hf] < T ? tq[hf] : 0) * q_dim + (size_t)(g * GQ + r % GQ) * HD;
   }
+  // Q as A fragments, k-step kk: {row g4, row g4 + 8} x {dims 16 kk + 2 c4 (+1), + 8}, hi and lo
+  uint32_t qa[KS][4], ql[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int hf = i & 1, d = 16 * kk + 8 * (i >> 1) + 2 * c4;
+      float2 x = make_float2(0.f, 0.f);
+      if (tq[hf] < T) x = *reinterpret_cast<const float2*>(qrow[hf] + d);
+      split_f16x2(x.x, x.y, qa[kk][i], ql[kk][i]);
+    }
+
   const float rsq = sqrtf((float)HD);  // scores are q.k / sqrt(head_dim), as in the decode kernel
-  float m[kPaRows], lsum[kPaRows], o[kPaRows][DPL];
+  float o[NT][4];
 #pragma unroll
-  for (int r = 0; r < kPaRows; ++r) {
-    m[r] = -INFINITY;
-    lsum[r] = 0.f;
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) o[r][d] = 0.f;
-  }
-  float* Pw = Ps + (size_t)warp * kPaRows * kPaKeys;
+    for (int i = 0; i < 4; ++i) o[nt][i] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
 
   for (int k0 = 0; k0 < kend; k0 += kPaKeys) {
     __syncthreads();  // the previous tile is no longer read
-    for (int e = threadIdx.x; e < kPaKeys * (HD / 8); e += blockDim.x) {
-      const int kk = e / (HD / 8), c = e % (HD / 8);
+    for (int e = threadIdx.x; e < kPaKeys * CPR; e += blockDim.x) {
+      const int kk = e / CPR, c = e % CPR;
       uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
       if (k0 + kk < kend) {
         kv = *reinterpret_cast<const uint4*>(kg + (size_t)(k0 + kk) * HD + c * 8);
         vv = *reinterpret_cast<const uint4*>(vg + (size_t)(k0 + kk) * HD + c * 8);
       }
-      *reinterpret_cast<uint4*>(Ks + kk * KS + c * 8) = kv;
-      *reinterpret_cast<uint4*>(Vs + kk * HD + c * 8) = vv;
+      *reinterpret_cast<uint4*>(Ks + kk * RB + c * 16) = kv;
+      *reinterpret_cast<uint4*>(Vs + kk * RB + c * 16) = vv;
     }
     __syncthreads();
-    // scores: rows x keys (k0 + lane, k0 + lane + 32)
-    float sc[kPaRows][2];
+
+    // S = Q . K^T: n-tile nt = keys k0 + 8 nt .. + 7; ldmatrix x4 gives the B fragments of n-tiles
+    // 2 np and 2 np + 1 (matrix lane / 8 = (keys +0 | +8) x (dims +0 | +8))
+    float s[8][4];
 #pragma unroll
-    for (int r = 0; r < kPaRows; ++r) sc[r][0] = sc[r][1] = 0.f;
-    for (int c = 0; c < HD / 8; ++c) {
-      float kf[2][8];
+    for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(Ks + (lane + 32 * j) * KS + c * 8);
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+      for (int i = 0; i < 4; ++i) s[nt][i] = 0.f;
+    {
+      const int key = 8 * ((lane >> 3) >> 1) + (lane & 7), hi = (lane >> 3) & 1;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(h2[i]);
-          kf[j][2 * i] = f.x;
-          kf[j][2 * i + 1] = f.y;
+      for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          uint32_t B[4];
+          ldsm_x4(B, ks_s + (16 * np + key) * RB + (2 * kk + hi) * 16);
+          mma_16816(s[2 * np], qa[kk], B[0], B[1]);
+          mma_16816(s[2 * np], ql[kk], B[0], B[1]);
+          mma_16816(s[2 * np + 1], qa[kk], B[2], B[3]);
+          mma_16816(s[2 * np + 1], ql[kk], B[2], B[3]);
         }
-      }
-#pragma unroll
-      for (int r = 0; r < kPaRows; ++r) {
-        const float4 qa = *reinterpret_cast<const float4*>(Qw + r * HD + c * 8);
-        const float4 qb4 = *reinterpret_cast<const float4*>(Qw + r * HD + c * 8 + 4);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          float acc = sc[r][j];
-          acc = fmaf(qa.x, kf[j][0], acc);
-          acc = fmaf(qa.y, kf[j][1], acc);
-          acc = fmaf(qa.z, kf[j][2], acc);
-          acc = fmaf(qa.w, kf[j][3], acc);
-          acc = fmaf(qb4.x, kf[j][4], acc);
-          acc = fmaf(qb4.y, kf[j][5], acc);
-          acc = fmaf(qb4.z, kf[j][6], acc);
-          acc = fmaf(qb4.w, kf[j][7], acc);
-          sc[r][j] = acc;
-        }
-      }
     }
-    // causal mask, online softmax, probabilities to shared memory
+
+    // causal mask, online softmax: lane holds keys k0 + 8 nt + 2 c4 + e of rows g4 (i = e) and
+    // g4 + 8 (i = 2 + e); a row's four lanes (same g4) reduce with xor 1, 2
+    float alpha[2];
 #pragma unroll
-    for (int r = 0; r < kPaRows; ++r) {
-      const int t = q0 + warp * QW + r / GQ;
-      const int qp = pos0 + t;
-      float s0 = sc[r][0] / rsq, s1 = sc[r][1] / rsq;
-      if (t >= T || k0 + lane > qp) s0 = -INFINITY;
-      if (t >= T || k0 + lane + 32 > qp) s1 = -INFINITY;
-      const float mx = warp_max(fmaxf(s0, s1));
-      const float mn = fmaxf(m[r], mx);
-      float p0 = 0.f, p1 = 0.f, alpha = 1.f;
+    for (int hf = 0; hf < 2; ++hf) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = k0 + 8 * nt + 2 * c4 + e;
+          float v = s[nt][2 * hf + e] / rsq;
+          if (tq[hf] >= T || key > qpos[hf]) v = -INFINITY;
+          s[nt][2 * hf + e] = v;
+          mx = fmaxf(mx, v);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m[hf], mx);
+      alpha[hf] = 1.f;
+      float ps = 0.f;
       if (mn != -INFINITY) {
-        alpha = expf(m[r] - mn);  // 0 while m[r] is still -inf
-        p0 = s0 == -INFINITY ? 0.f : expf(s0 - mn);
-        p1 = s1 == -INFINITY ? 0.f : expf(s1 - mn);
-        m[r] = mn;
+        alpha[hf] = expf(m[hf] - mn);  // 0 while m[hf] is still -inf
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float v = s[nt][2 * hf + e];
+            const float pv = v == -INFINITY ? 0.f : expf(v - mn);
+            s[nt][2 * hf + e] = pv;
+            ps += pv;
+          }
+        m[hf] = mn;
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) s[nt][2 * hf] = s[nt][2 * hf + 1] = 0.f;
       }
-      lsum[r] = lsum[r] * alpha + p0 + p1;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) o[r][d] *= alpha;
-      Pw[r * kPaKeys + lane] = p0;
-      Pw[r * kPaKeys + lane + 32] = p1;
+      l[hf] = l[hf] * alpha[hf] + ps;  // this lane's share; the row's four lanes are summed at the end
     }
-    __syncwarp();
-    // o += P . V over the tile's keys
-    const int nk = min(kPaKeys, kend - k0);
-    for (int kk = 0; kk < nk; kk += 4) {
-      float vf[4][DPL];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (DPL == 4) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(Vs + (kk + u) * HD + lane * 4);
-          const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-          const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-          vf[u][0] = a0.x; vf[u][1 % DPL] = a0.y; vf[u][2 % DPL] = a1.x; vf[u][3 % DPL] = a1.y;
-        } else {
-          const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(Vs + (kk + u) * HD + lane * 2));
-          vf[u][0] = a0.x; vf[u][1 % DPL] = a0.y;
+    for (int nt = 0; nt < NT; ++nt) {
+      o[nt][0] *= alpha[0];
+      o[nt][1] *= alpha[0];
+      o[nt][2] *= alpha[1];
+      o[nt][3] *= alpha[1];
+    }
+
+    // O += P . V: k-step ks = keys 16 ks .. + 15; P's A fragment is S n-tiles 2 ks, 2 ks + 1;
+    // ldmatrix.trans x4 gives the B fragments of output n-tiles 2 np, 2 np + 1 (matrix lane / 8 =
+    // (keys +0 | +8) x (dims +0 | +8))
+    {
+      const int key = 8 * ((lane >> 3) & 1) + (lane & 7), hi = (lane >> 3) >> 1;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t ph[4], pl[4];
+        split_f16x2(s[2 * ks][0], s[2 * ks][1], ph[0], pl[0]);
+        split_f16x2(s[2 * ks][2], s[2 * ks][3], ph[1], pl[1]);
+        split_f16x2(s[2 * ks + 1][0], s[2 * ks + 1][1], ph[2], pl[2]);
+        split_f16x2(s[2 * ks + 1][2], s[2 * ks + 1][3], ph[3], pl[3]);
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+          uint32_t B[4];
+          ldsm_x4_trans(B, vs_s + (16 * ks + key) * RB + (2 * np + hi) * 16);
+          mma_16816(o[2 * np], ph, B[0], B[1]);
+          mma_16816(o[2 * np], pl, B[0], B[1]);
+          mma_16816(o[2 * np + 1], ph, B[2], B[3]);
+          mma_16816(o[2 * np + 1], pl, B[2], B[3]);
         }
       }
-#pragma unroll
-      for (int r = 0; r < kPaRows; ++r) {
-        const float4 pp = *reinterpret_cast<const float4*>(Pw + r * kPaKeys + kk);
-#pragma unroll
-        for (int d = 0; d < DPL; ++d) {
-          float acc = o[r][d];
-          acc = fmaf(pp.x, vf[0][d], acc);
-          acc = fmaf(pp.y, vf[1][d], acc);
-          acc = fmaf(pp.z, vf[2][d], acc);
-          acc = fmaf(pp.w, vf[3][d], acc);
-          o[r][d] = acc;
-        }
-      }
     }
-    __syncwarp();  // Pw is rewritten by the next tile
   }
-  // normalise and store
+
+  // normalise and store: lane holds dims 8 nt + 2 c4 (+1) of rows g4 (i = 0, 1) and g4 + 8 (i = 2, 3)
 #pragma unroll
-  for (int r = 0; r < kPaRows; ++r) {
-    const int t = q0 + warp * QW + r / GQ;
-    const float l = warp_sum(lsum[r]);
-    if (t < T) {
-      __half* dst = out + (size_t)t * q_dim + (size_t)(g * GQ + r % GQ) * HD + lane * DPL;
+  for (int hf = 0; hf < 2; ++hf) {
+    float lt = l[hf];
+    lt += __shfl_xor_sync(0xffffffffu, lt, 1);
+    lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+    if (tq[hf] < T) {
+      const int r = g4 + 8 * hf;
+      __half* dst = out + (size_t)tq[hf] * q_dim + (size_t)(g * GQ + r % GQ) * HD + 2 * c4;
+      const float inv = 1.f / lt;
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) dst[d] = __float2half_rn(o[r][d] / l);
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<__half2*>(dst + 8 * nt) = __floats2half2_rn(o[nt][2 * hf] * inv, o[nt][2 * hf + 1] * inv);
     }
   }
 }
@@ -279,10 +307,7 @@ cudaError_t prefill_attention(const float* q, const __half* k_cache, const __hal
   const int gq = n_heads / n_kv_heads;
   const void* fn = head_dim == 128 ? pick_pa<128>(gq) : head_dim == 64 ? pick_pa<64>(gq) : nullptr;
   if (!fn) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)8 * kPaRows * head_dim * 4 + (size_t)8 * kPaRows * kPaKeys * 4 +
-                      (size_t)kPaKeys * (head_dim + 8) * 2 + (size_t)kPaKeys * head_dim * 2;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  const size_t smem = (size_t)2 * kPaKeys * pa_row_bytes(head_dim);
   const int qb = 8 * (kPaRows / gq);
   const dim3 grid((T + qb - 1) / qb, n_kv_heads);
   void* args[] = {&q, &k_cache, &v_cache, &out, &T, &pos0, &n_heads, &max_seq_len};
