@@ -115,6 +115,15 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// 16-byte global -> shared copy through L2 only (cp.async, completion per thread via commit/wait
+// groups); src_bytes 0 writes zeros (src must still be a valid address).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, unsigned src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // 2-D tiled TMA load of one box of `map` at element coordinates (x inner, y outer) into shared
 // memory, completing on `bar`.  x times the element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d_s(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {

@@ -94,7 +94,7 @@ cudaError_t prefill_qkv_post(const float* qkv, int T, int pos0, int q_rows, int 
 // heads of its kv head.  Per key tile of 64 slots a warp works on the tensor cores (mma.sync
 // m16n8k16, fp32 accumulate), flash-attention style:
 //   S[16 rows][64 keys] = Q . K^T     (q split into fp16 hi + lo parts: the products keep ~22 bits)
-//   causal mask, online softmax (running max / sum per row, rescaling O when the max grows)
+//   causal mask, online softmax in base 2 (running max / sum per row, rescaling O when the max grows)
 //   O[16 rows][HD] += P . V           (p split the same way)
 // The S accumulator fragments become the P operand fragments in registers (same row / column
 // layout).  K and V rows are staged with a padded stride (an odd multiple of 16 bytes) so the eight
@@ -117,9 +117,9 @@ __global__ void __launch_bounds__(256, 1)
   constexpr int RB = pa_row_bytes(HD);
   constexpr int CPR = HD / 8;       // 16-byte chunks per cache row
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* Ks = smem;                  // [64][RB]
-  unsigned char* Vs = smem + kPaKeys * RB;   // [64][RB]
-  const uint32_t ks_s = smem_u32(Ks), vs_s = smem_u32(Vs);
+  // two buffers (double-buffered key tiles), each K [64][RB] then V [64][RB]
+  constexpr uint32_t TB = 2u * kPaKeys * RB;
+  const uint32_t sm_s = smem_u32(smem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g4 = lane >> 2, c4 = lane & 3;
@@ -155,7 +155,8 @@ __global__ void __launch_bounds__(256, 1)
       split_f16x2(x.x, x.y, qa[kk][i], ql[kk][i]);
     }
 
-  const float rsq = sqrtf((float)HD);  // scores are q.k / sqrt(head_dim), as in the decode kernel
+  // scores q.k / sqrt(head_dim) are kept in base 2: t = q.k * log2(e) / sqrt(head_dim), p = 2^(t - max)
+  const float sl2 = 1.4426950408889634f / sqrtf((float)HD);
   float o[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -163,19 +164,31 @@ __global__ void __launch_bounds__(256, 1)
     for (int i = 0; i < 4; ++i) o[nt][i] = 0.f;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
 
-  for (int k0 = 0; k0 < kend; k0 += kPaKeys) {
-    __syncthreads();  // the previous tile is no longer read
+  // key tile it -> buffer it & 1; slots past kend are zero-filled
+  auto stage = [&](int it) {
+    const int kb0 = it * kPaKeys;
+    const uint32_t kbuf = sm_s + (uint32_t)(it & 1) * TB, vbuf = kbuf + kPaKeys * RB;
     for (int e = threadIdx.x; e < kPaKeys * CPR; e += blockDim.x) {
       const int kk = e / CPR, c = e % CPR;
-      uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
-      if (k0 + kk < kend) {
-        kv = *reinterpret_cast<const uint4*>(kg + (size_t)(k0 + kk) * HD + c * 8);
-        vv = *reinterpret_cast<const uint4*>(vg + (size_t)(k0 + kk) * HD + c * 8);
-      }
-      *reinterpret_cast<uint4*>(Ks + kk * RB + c * 16) = kv;
-      *reinterpret_cast<uint4*>(Vs + kk * RB + c * 16) = vv;
+      const bool in = kb0 + kk < kend;
+      const size_t off = in ? (size_t)(kb0 + kk) * HD + c * 8 : 0;
+      cp_async16(kbuf + kk * RB + c * 16, kg + off, in ? 16u : 0u);
+      cp_async16(vbuf + kk * RB + c * 16, vg + off, in ? 16u : 0u);
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  const int ntile = (kend + kPaKeys - 1) / kPaKeys;
+  stage(0);
+  for (int it = 0; it < ntile; ++it) {
+    const int k0 = it * kPaKeys;
+    if (it + 1 < ntile) {
+      stage(it + 1);  // its buffer was released by the barrier at the end of iteration it - 1
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // every thread's copies of tile it have landed
+    const uint32_t ks_s = sm_s + (uint32_t)(it & 1) * TB, vs_s = ks_s + kPaKeys * RB;
 
     // S = Q . K^T: n-tile nt = keys k0 + 8 nt .. + 7; ldmatrix x4 gives the B fragments of n-tiles
     // 2 np and 2 np + 1 (matrix lane / 8 = (keys +0 | +8) x (dims +0 | +8))
@@ -187,16 +200,22 @@ __global__ void __launch_bounds__(256, 1)
     {
       const int key = 8 * ((lane >> 3) >> 1) + (lane & 7), hi = (lane >> 3) & 1;
 #pragma unroll
-      for (int kk = 0; kk < KS; ++kk)
+      for (int kk = 0; kk < KS; ++kk) {
+        // the eight hi products first, then the eight lo ones: dependent mma are 8 apart
+        uint32_t B[4][4];
+#pragma unroll
+        for (int np = 0; np < 4; ++np) ldsm_x4(B[np], ks_s + (16 * np + key) * RB + (2 * kk + hi) * 16);
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
-          uint32_t B[4];
-          ldsm_x4(B, ks_s + (16 * np + key) * RB + (2 * kk + hi) * 16);
-          mma_16816(s[2 * np], qa[kk], B[0], B[1]);
-          mma_16816(s[2 * np], ql[kk], B[0], B[1]);
-          mma_16816(s[2 * np + 1], qa[kk], B[2], B[3]);
-          mma_16816(s[2 * np + 1], ql[kk], B[2], B[3]);
+          mma_16816(s[2 * np], qa[kk], B[np][0], B[np][1]);
+          mma_16816(s[2 * np + 1], qa[kk], B[np][2], B[np][3]);
         }
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          mma_16816(s[2 * np], ql[kk], B[np][0], B[np][1]);
+          mma_16816(s[2 * np + 1], ql[kk], B[np][2], B[np][3]);
+        }
+      }
     }
 
     // causal mask, online softmax: lane holds keys k0 + 8 nt + 2 c4 + e of rows g4 (i = e) and
@@ -210,7 +229,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int key = k0 + 8 * nt + 2 * c4 + e;
-          float v = s[nt][2 * hf + e] / rsq;
+          float v = s[nt][2 * hf + e] * sl2;
           if (tq[hf] >= T || key > qpos[hf]) v = -INFINITY;
           s[nt][2 * hf + e] = v;
           mx = fmaxf(mx, v);
@@ -221,13 +240,13 @@ __global__ void __launch_bounds__(256, 1)
       alpha[hf] = 1.f;
       float ps = 0.f;
       if (mn != -INFINITY) {
-        alpha[hf] = expf(m[hf] - mn);  // 0 while m[hf] is still -inf
+        alpha[hf] = exp2f(m[hf] - mn);  // 0 while m[hf] is still -inf
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const float v = s[nt][2 * hf + e];
-            const float pv = v == -INFINITY ? 0.f : expf(v - mn);
+            const float pv = v == -INFINITY ? 0.f : exp2f(v - mn);
             s[nt][2 * hf + e] = pv;
             ps += pv;
           }
@@ -258,17 +277,24 @@ __global__ void __launch_bounds__(256, 1)
         split_f16x2(s[2 * ks][2], s[2 * ks][3], ph[1], pl[1]);
         split_f16x2(s[2 * ks + 1][0], s[2 * ks + 1][1], ph[2], pl[2]);
         split_f16x2(s[2 * ks + 1][2], s[2 * ks + 1][3], ph[3], pl[3]);
+        // hi products for every output n-tile, then lo: dependent mma are NT apart
 #pragma unroll
         for (int np = 0; np < NT / 2; ++np) {
           uint32_t B[4];
           ldsm_x4_trans(B, vs_s + (16 * ks + key) * RB + (2 * np + hi) * 16);
           mma_16816(o[2 * np], ph, B[0], B[1]);
-          mma_16816(o[2 * np], pl, B[0], B[1]);
           mma_16816(o[2 * np + 1], ph, B[2], B[3]);
+        }
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+          uint32_t B[4];
+          ldsm_x4_trans(B, vs_s + (16 * ks + key) * RB + (2 * np + hi) * 16);
+          mma_16816(o[2 * np], pl, B[0], B[1]);
           mma_16816(o[2 * np + 1], pl, B[2], B[3]);
         }
       }
     }
+    __syncthreads();  // tile it's buffer is free for tile it + 2
   }
 
   // normalise and store: lane holds dims 8 nt + 2 c4 (+1) of rows g4 (i = 0, 1) and g4 + 8 (i = 2, 3)
@@ -307,7 +333,9 @@ cudaError_t prefill_attention(const float* q, const __half* k_cache, const __hal
   const int gq = n_heads / n_kv_heads;
   const void* fn = head_dim == 128 ? pick_pa<128>(gq) : head_dim == 64 ? pick_pa<64>(gq) : nullptr;
   if (!fn) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)2 * kPaKeys * pa_row_bytes(head_dim);
+  const size_t smem = (size_t)4 * kPaKeys * pa_row_bytes(head_dim);
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
   const int qb = 8 * (kPaRows / gq);
   const dim3 grid((T + qb - 1) / qb, n_kv_heads);
   void* args[] = {&q, &k_cache, &v_cache, &out, &T, &pos0, &n_heads, &max_seq_len};
