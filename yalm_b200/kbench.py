@@ -120,13 +120,33 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
             "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
 
 
+def bench_prefill_attention(nh, nkv, hd, T, iters, seed=0):
+    """Causal attention of a T-token prompt (yb_prefill_attention_dev); the caches fit in L2, as in
+    the prefill where each layer's K/V were just written."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn(T, nh * hd, device="cuda", generator=g)
+    k = torch.randn(nkv, T, hd, device="cuda", generator=g).half()
+    v = torch.randn(nkv, T, hd, device="cuda", generator=g).half()
+    out = torch.zeros(T * nh * hd, dtype=torch.float16, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def fn(i):
+        _lib.call("yb_prefill_attention_dev", _p(out), _p(q), _p(k), _p(v), T, 0, nh, nkv, hd, T, stream)
+    ms = _time(fn, iters)
+    flop = 4.0 * nh * hd * T * (T + 1) / 2  # q.k and p.v over the causal triangle
+    return {"kernel": "prefill_attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "tokens": T,
+            "us": round(ms * 1000, 2), "tflops": round(flop / (ms / 1000) / 1e12, 1)}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default="all", choices=["gemv", "gateup", "qkv", "attention", "all"])
+    ap.add_argument("--kernel", default="all", choices=["gemv", "gateup", "qkv", "attention", "prefill_attention", "all"])
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--quick", action="store_true", help="one shape per kernel (for profiler captures)")
     ap.add_argument("--kv-lens", default="", help="attention: comma-separated kv_len values")
     ap.add_argument("--msl", type=int, default=0, help="attention: cache capacity (default: kv_len)")
+    ap.add_argument("--tokens", default="", help="prefill_attention: comma-separated prompt lengths")
     args = ap.parse_args(argv)
     import torch
     torch.cuda.set_device(0)
@@ -145,6 +165,10 @@ def main(argv=None):
             lens = [int(v) for v in args.kv_lens.split(",")]
         for kv in lens:
             rows.append(bench_attention(32, 8, 128, kv, args.iters, msl=args.msl or None))
+    if args.kernel in ("prefill_attention", "all"):
+        lens = [int(v) for v in args.tokens.split(",")] if args.tokens else ([1024] if args.quick else [1024, 3202])
+        for t in lens:
+            rows.append(bench_prefill_attention(32, 8, 128, t, max(3, args.iters // 20)))
     for r in rows:
         print(json.dumps(r))
 
