@@ -266,7 +266,8 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
         a.pf_bytes = (long long)c.dim * e->q_rows * e->esz;
       }
       timeline(&a.trace, &a.trace_stride);
-      YB_CK(gemv_launch(a.tp_ll ? e->plan_qkv_tp : e->plan_qkv, a, s, true, pf));
+      YB_CK(gemv_launch(a.tp_ll ? e->plan_qkv_tp : e->plan_qkv, a, s, true,
+                        e->tune.l2_prefetch_qkv >= 0 ? e->tune.l2_prefetch_qkv : pf));
     }
     // ---- attention
     {
@@ -298,7 +299,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
         a.y = x_cur;
       }
       timeline(&a.trace, &a.trace_stride);
-      YB_CK(gemv_launch(e->plan_wo, a, s, true, pf));
+      YB_CK(gemv_launch(e->plan_wo, a, s, true, e->tune.l2_prefetch_wo >= 0 ? e->tune.l2_prefetch_wo : pf));
     }
     // ---- gate/up (+ RMSNorm, SwiGLU)
     {

@@ -492,6 +492,8 @@ LaunchTuning LaunchTuning::from_env() {
         else if (k == "budget" && v >= 16384) t.smem_budget = v;
         else if (k == "slots" && v >= 2) t.max_slots = v;
         else if (k == "l2pf" && v >= 0) t.l2_prefetch_stages = v;
+        else if (k == "l2wo" && v >= 0) t.l2_prefetch_wo = v;
+        else if (k == "l2qkv" && v >= 0) t.l2_prefetch_qkv = v;
         else if (k == "ctas" && v >= 1 && v <= 8) t.ctas_per_sm = v;
         else if (k == "pstatic" && v >= 0 && v <= 100) t.persist_static_pct = v;
         else if (k == "pfq" && v >= 0) t.prefetch_qkv = v != 0;

@@ -17,13 +17,15 @@ struct LaunchTuning {
   int smem_budget = 100000;        // per-CTA dynamic shared memory; two CTAs fit on one SM
   int max_slots = 8;               // ring depth cap
   int l2_prefetch_stages = 0;      // stages beyond the ring warmed into L2 before griddepcontrol.wait (measured: off is faster)
+  int l2_prefetch_wo = -1;         // the same for the wo matvec alone (-1: l2_prefetch_stages)
+  int l2_prefetch_qkv = -1;        // the same for the QKV matvec alone (-1: l2_prefetch_stages)
   int ctas_per_sm = 2;              // GEMV grid = min(stages, SMs * ctas_per_sm)
   bool prefetch_qkv = false;        // graph executor: W2 kernels warm L2 with the next layer's QKV rows
   bool prefetch_wo = false;         // graph executor: QKV kernels warm L2 with the layer's Wo
   int persist_static_pct = 100;     // persistent executor: statically split share of each matvec
   int persist_claim_ctrs = 8;       // persistent executor: counters for the dynamically claimed rest
 
-  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,ctas=2" (read once
+  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2" (read once
   // per process) for tuning sweeps.
   static LaunchTuning from_env();
 };
