@@ -4,10 +4,21 @@
 //   s_t = q_h . k_t / sqrt(head_dim),  p = softmax(s[0..kv_len)),  out_h = sum_t p_t v_t
 // (src/infer.cpp:218-250; the CUDA kernel attn_fused, src/infer.cu:625-667, runs one CTA per q head
 // and reads each K/V head once per q head).  Here one CTA serves all GQ query heads of a kv head for
-// one slice of cache slots, so K/V bytes cross HBM once per kv head.  Slices are staged into shared
-// memory with 1-D TMA (K and V rows are contiguous [slot][head_dim]); each CTA keeps a running
-// max / sum / output per head (online softmax), writes (m, l, o) for its slice, and the last CTA of
-// a kv head to finish merges the slices with a log-sum-exp rescale and writes the head outputs.
+// one slice of at most 128 cache slots, so K/V bytes cross HBM once per kv head:
+//
+//   * after the wait on the QKV kernel (whose producers have already warmed L2 with this layer's
+//     K/V rows) the slice's K and V rows are copied to shared memory with cp.async, rows padded to
+//     an odd multiple of 16 bytes so one ldmatrix touches eight bank groups;
+//   * each of the 8 warps takes 16 slots and works on the tensor cores (mma.sync m16n8k16, fp32
+//     accumulate): S^T[16 slots][8 heads] = K . Q^T, a softmax over its 16 slots per head, then
+//     O^T[head_dim][8 heads] = V^T . P^T.  q and p are fp32 values split into an fp16 value and its
+//     fp16 remainder (two mma passes), so the products keep about 22 bits, as the fp32 loops do;
+//   * the 8 warps' (max, sum, o) are combined in shared memory; a slice of a longer cache writes its
+//     (m, l, o) record and the last CTA of a kv head to finish merges the slices with a log-sum-exp
+//     rescale and writes the head outputs.
+//
+// The work is a few hundred mma per CTA: the kernel is bound by the K/V read and by latency, and
+// the tensor cores serve to keep the instruction count (and so the latency) small.
 #include "attention.cuh"
 #include "launch.h"
 
@@ -18,24 +29,128 @@ namespace yb {
 constexpr int kAttnThreads = 256;
 // Slice partial record: o[0..HD), m at HD, l at HD + 1, padded to a 16-byte multiple.
 constexpr int attn_part_stride(int hd) { return hd + 4; }
-constexpr int kAttnSub = 64;  // cache slots per staged sub-chunk (8 warps x 8 slots)
+constexpr int kAttnSub = 64;  // minimum slice of a cache longer than one CTA's capacity
+
+// One warp's group of 16 staged slots (rows r0 .. r0 + 15 of the K rows at shared address kb and
+// the V rows at vb, RB bytes apart; my_n of them valid): scores, softmax and output on the tensor
+// cores, then the group's (o, m, l) per head into the combine buffer (rw: [GQ][HD + 4], rm, rl:
+// [GQ]).  Fragment layouts: see mma_16816 in common.cuh.
+template <int HD, int GQ, int RB>
+__device__ __forceinline__ void attn_group(uint32_t kb, uint32_t vb, int r0, int my_n, int lane,
+                                           const uint32_t (&qh)[HD / 16][2], const uint32_t (&ql)[HD / 16][2],
+                                           float* rw, float* rm, float* rl) {
+  constexpr int KS = HD / 16;
+  constexpr int RS = HD + 4;
+  const int gh = lane >> 2, c4 = lane & 3;
+  // S^T = K . Q^T over HD in KS k-steps; four independent accumulators (hi / lo x even / odd step)
+  float acc[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[u][i] = 0.f;
+  {
+    // ldmatrix rows: matrix lane / 8 = (slots 0-7 | 8-15) x (dims +0 | +8) in A-fragment order
+    const int lr = r0 + 8 * ((lane >> 3) & 1) + (lane & 7);
+    const int lc = lane >> 4;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      uint32_t A[4];
+      ldsm_x4(A, kb + lr * RB + (2 * kk + lc) * 16);
+      mma_16816(acc[(kk & 1) * 2], A, qh[kk][0], qh[kk][1]);
+      mma_16816(acc[(kk & 1) * 2 + 1], A, ql[kk][0], ql[kk][1]);
+    }
+  }
+  // lane holds slots gh (i = 0, 1) and gh + 8 (i = 2, 3) of heads 2 c4 + (i & 1)
+  const float scale = 1.0f / sqrtf((float)HD);
+  const bool v0 = gh < my_n, v1 = gh + 8 < my_n;
+  float s[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float t = ((acc[0][i] + acc[2][i]) + (acc[1][i] + acc[3][i])) * scale;
+    s[i] = (i < 2 ? v0 : v1) ? t : -INFINITY;
+  }
+  float m0 = fmaxf(s[0], s[2]), m1 = fmaxf(s[1], s[3]);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+  }
+  // slot 0 of the group is always valid, so m0, m1 are finite
+  const float p0 = v0 ? expf(s[0] - m0) : 0.f, p1 = v0 ? expf(s[1] - m1) : 0.f;
+  const float p2 = v1 ? expf(s[2] - m0) : 0.f, p3 = v1 ? expf(s[3] - m1) : 0.f;
+  float l0 = p0 + p2, l1 = p1 + p3;
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+
+  // P^T as the B operand of the output mma: the lane's (slot, head pair) rows transposed to
+  // (head, slot pair) by movmatrix, hi and lo parts
+  uint32_t x0h, x0l, x1h, x1l;
+  split_f16x2(p0, p1, x0h, x0l);
+  split_f16x2(p2, p3, x1h, x1l);
+  const uint32_t bh0 = movm_trans(x0h), bh1 = movm_trans(x1h);
+  const uint32_t bl0 = movm_trans(x0l), bl1 = movm_trans(x1l);
+
+  // O^T = V^T . P^T: m-tile mt covers dims 16 mt .. 16 mt + 15
+  float o[KS][4];
+  {
+    // ldmatrix.trans rows: matrix lane / 8 = (slots 0-7 | 8-15) x (dims +0 | +8), A order
+    const int vr = r0 + 8 * (lane >> 4) + (lane & 7);
+    const int vc = (lane >> 3) & 1;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[mt][i] = 0.f;
+      uint32_t A[4];
+      ldsm_x4_trans(A, vb + vr * RB + (2 * mt + vc) * 16);
+      mma_16816(o[mt], A, bh0, bh1);
+      mma_16816(o[mt], A, bl0, bl1);
+    }
+  }
+
+  // lane holds dims 16 mt + gh (+8) of heads 2 c4, 2 c4 + 1
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int h = 2 * c4 + e;
+    if (h < GQ) {
+      float* r = rw + h * RS;
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+        r[16 * mt + gh] = o[mt][e];
+        r[16 * mt + gh + 8] = o[mt][2 + e];
+      }
+      if (gh == 0) {
+        rm[h] = e ? m1 : m0;
+        rl[h] = e ? l1 : l0;
+      }
+    }
+  }
+}
 
 template <int HD, int GQ>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
-  constexpr int DPL = HD / 32;                  // head dims per lane
-  constexpr int NV = (8 * GQ < 32) ? 8 * GQ : 32;  // partial scores per reduce-scatter round
-  constexpr int ROUNDS = (8 * GQ + 31) / 32;
-  constexpr int PR = NV / GQ;                    // slots per round per warp
-  constexpr int LOG_NV = (NV == 8) ? 3 : (NV == 16) ? 4 : 5;
-  constexpr int SLOTS = 2;                       // sub-chunks per CTA (capacity 128 slots)
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const AttnArgs a) {
+  static_assert(GQ >= 1 && GQ <= 8, "the score mma has 8 head columns");
+  constexpr int KS = HD / 16;                // k-steps of the score mma = m-tiles of the output mma
+  constexpr int CH = HD / 8;                 // 16-byte chunks per cache row
+  constexpr int RB = attn_row_bytes(HD);     // padded shared-memory row
+  constexpr int SLOTS = 2;                   // the merge barrier is bar[SLOTS]
   constexpr int PS = attn_part_stride(HD);
+  constexpr int RS = HD + 4;                 // warp-combine row stride (floats)
+  constexpr int DPL = HD / 32;               // head dims per lane in the slice merge
 
   extern __shared__ __align__(128) unsigned char smem[];
-  __half* Ks = reinterpret_cast<__half*>(smem);                         // [SLOTS][64][HD]
-  __half* Vs = Ks + SLOTS * kAttnSub * HD;                              // [SLOTS][64][HD]
+  // [0, region): K rows [128][RB] then V rows [128][RB], or the slice records of the merge
+  const uint32_t ks_s = smem_u32(smem), vs_s = ks_s + kAttnCapacity * RB;
   const bool merge_smem = attn_merge_in_smem(HD, GQ, gridDim.x);
-  float* S = reinterpret_cast<float*>(smem + attn_region_bytes(HD, GQ, gridDim.x));  // [2][GQ][64]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(S + 2 * GQ * kAttnSub);  // [SLOTS] stages, [SLOTS] merge
+  const size_t region = attn_region_bytes(HD, GQ, gridDim.x);
+  float* red = reinterpret_cast<float*>(smem + region);  // [8][GQ][RS]
+  float* red_m = red + 8 * GQ * RS;  // [8][GQ] warp max
+  float* red_l = red_m + 8 * GQ;     // [8][GQ] warp sum
+  float* wgt = red_l + 8 * GQ;       // [8][GQ] warp weight exp(m_w - M)
+  float* tot = wgt + 8 * GQ;         // [GQ] CTA max M, [GQ] CTA sum L
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + region + (attn_red_bytes(HD, GQ) + 15) / 16 * 16);
   __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -44,273 +159,126 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   pdl_trigger();
   unsigned long long* const tr =
       a.trace ? a.trace + (size_t)blockIdx.y * gridDim.x * a.trace_stride : nullptr;  // row of this CTA
-  if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 0);
-
-  const int s_max = gridDim.x;
-  // A cache of at most one CTA's capacity goes to slice 0 alone (no merge); longer ones split into
-  // slices of at least one staged sub-chunk. Slice sidx of a cache of len slots covers [t0, t1) in
-  // n_sub sub-chunks (0 = inactive).
-  auto partition = [&](int len, int& t0_, int& t1_, int& nsub_, int& nact_) {
-    int ch = (len + s_max - 1) / s_max;
-    ch = ((ch + 15) / 16) * 16;
-    if (len <= kAttnCapacity) ch = kAttnCapacity;
-    else if (ch < kAttnSub) ch = kAttnSub;
-    nact_ = (len + ch - 1) / ch;
-    t0_ = sidx * ch;
-    t1_ = min(len, t0_ + ch);
-    nsub_ = t0_ < len ? (t1_ - t0_ + kAttnSub - 1) / kAttnSub : 0;
-  };
-  const __half* kg = a.k_cache + (size_t)g * a.max_seq_len * HD;
-  const __half* vg = a.v_cache + (size_t)g * a.max_seq_len * HD;
-  auto issue = [&](int c_begin, int c_end, int j) {
-    const int c0 = c_begin + j * kAttnSub;
-    const int cn = min(kAttnSub, c_end - c0);
-    const unsigned bytes = (unsigned)cn * HD * 2u;
-    mbar_arrive_expect_tx(&bar[j], 2u * bytes);
-    bulk_g2s_nohint(Ks + (size_t)j * kAttnSub * HD, kg + (size_t)c0 * HD, bytes, &bar[j]);
-    bulk_g2s_nohint(Vs + (size_t)j * kAttnSub * HD, vg + (size_t)c0 * HD, bytes, &bar[j]);
-  };
-
-  // Before the wait on the QKV kernel: stage the cache slots of this slice for the kv_len the step
-  // state shows now (normally this step's, possibly the previous step's: it is only a hint).  All
-  // slots but the one the QKV kernel is appending (and, past the context, the two re-rotated sink
-  // keys) already hold their final values; those few rows are patched from global memory below.
-  int h0, h1, hsub, hact;
-  {
-    int hlen = a.step ? *reinterpret_cast<const volatile int*>(&a.step->kv_len) : a.kv_len;
-    hlen = hlen < 1 ? 1 : (hlen > a.max_seq_len ? a.max_seq_len : hlen);
-    partition(hlen, h0, h1, hsub, hact);
-  }
   if (threadIdx.x == 0) {
-    for (int j = 0; j <= SLOTS; ++j) mbar_init(&bar[j], 1);
+    timeline_stamp(tr, a.trace_stride, 0);
+    mbar_init(&bar[SLOTS], 1);
     mbar_fence_init();
-    for (int j = 0; j < hsub; ++j) issue(h0, h1, j);
   }
 
   pdl_wait();  // q and the newest K/V slot come from the QKV kernel
   if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 1);
 
   const int kv_len = a.step ? a.step->kv_len : a.kv_len;
-  const int kv_pos = a.step ? a.step->kv_pos : -1;
-  const int kv_sink = a.step ? a.step->kv_sink : 0;
-  int t0, t1, n_sub, n_act;
-  partition(kv_len, t0, t1, n_sub, n_act);
-  // the staged rows can be used when they cover the slice, apart from the appended slot
-  const bool reuse = n_sub == hsub && t0 == h0 && (t1 <= h1 || (t1 == h1 + 1 && kv_pos == h1));
-  if (n_sub == 0) {
-    // inactive slice (not counted by the merge): let any staged copy land before leaving
-    if (threadIdx.x == 0)
-      for (int j = 0; j < hsub; ++j) mbar_wait(&bar[j], 0, a.status);
-    return;
-  }
+  const int s_max = gridDim.x;
+  // A cache of at most one CTA's capacity goes to slice 0 alone (no merge); longer ones split into
+  // slices of at least kAttnSub slots. Slice sidx covers [t0, t1); n_act slices are active.
+  int ch = (kv_len + s_max - 1) / s_max;
+  ch = ((ch + 15) / 16) * 16;
+  if (kv_len <= kAttnCapacity) ch = kAttnCapacity;
+  else if (ch < kAttnSub) ch = kAttnSub;
+  const int n_act = (kv_len + ch - 1) / ch;
+  const int t0 = sidx * ch;
+  const int t1 = min(kv_len, t0 + ch);
+  if (t0 >= kv_len) return;  // inactive slice (not counted by the merge)
   const int n = t1 - t0;
-  // a sub-chunk whose stale staging had to be replaced completes its barrier's second phase
-  if (!reuse && threadIdx.x == 0) {
-    for (int j = 0; j < hsub; ++j) mbar_wait(&bar[j], 0, a.status);
-    for (int j = 0; j < n_sub; ++j) issue(t0, t1, j);
-  }
+  const int nw = (n + 15) / 16;  // warps with slots
 
-  // Rows this step's QKV kernel wrote after the staging was issued (src/infer.cpp:296-325): warp 0
-  // loads the appended K/V slot, warp 1 the re-rotated sink keys, together with q below; they are
-  // stored over the staged copies once their sub-chunk has landed.
-  constexpr int CH = HD / 8;  // 16-byte chunks per row
-  uint4 patch = make_uint4(0u, 0u, 0u, 0u);
-  int patch_row = -1, patch_col = 0;
-  bool patch_k = true;
-  if (reuse && a.step) {
-    if (warp == 0 && lane < 2 * CH && kv_pos >= t0 && kv_pos < t1) {
-      patch_k = lane < CH;
-      patch_col = lane % CH;
-      patch_row = kv_pos;
-    } else if (warp == 1 && lane < kv_sink * CH && lane / CH >= t0 && lane / CH < t1) {
-      patch_row = lane / CH;
-      patch_col = lane % CH;
+  // K and V rows [t0, t1) of this kv head; V rows up to the last warp's 16-slot boundary are
+  // zero-filled so 0 * v stays 0 (K rows there are masked out of the softmax)
+  {
+    const __half* kg = a.k_cache + ((size_t)g * a.max_seq_len + t0) * HD;
+    const __half* vg = a.v_cache + ((size_t)g * a.max_seq_len + t0) * HD;
+    for (int e = threadIdx.x; e < nw * 16 * CH; e += kAttnThreads) {
+      const int r = e / CH, c = e % CH;
+      const bool in = r < n;
+      const size_t off = in ? (size_t)r * HD + c * 8 : 0;
+      if (in) cp_async16(ks_s + r * RB + c * 16, kg + off, 16u);
+      cp_async16(vs_s + r * RB + c * 16, vg + off, in ? 16u : 0u);
     }
-    if (patch_row >= 0)
-      patch = __ldcg(reinterpret_cast<const uint4*>((patch_k ? kg : vg) + (size_t)patch_row * HD + patch_col * 8));
+    cp_async_commit();
   }
 
-  // q for the GQ heads of this kv group, this lane's DPL dims
-  float qr[GQ][DPL];
+  // q of the GQ heads as the B operand of the score mma: lane (gh = lane / 4, c4 = lane % 4) holds
+  // head gh, dims 16 kk + 2 c4 (+1) and 16 kk + 8 + 2 c4 (+1), as hi and lo fp16 pairs
+  const int gh = lane >> 2, c4 = lane & 3;
+  uint32_t qh[KS][2], ql[KS][2];
+  {
+    const float* qp = a.q + (size_t)(g * GQ + (gh < GQ ? gh : 0)) * HD + 2 * c4;
 #pragma unroll
-  for (int h = 0; h < GQ; ++h)
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) qr[h][d] = a.q[(size_t)(g * GQ + h) * HD + lane * DPL + d];
-  const float rsq = sqrtf((float)HD);
-
-  float m_run[GQ], l_w[GQ], o_w[GQ][DPL];
-#pragma unroll
-  for (int h = 0; h < GQ; ++h) {
-    m_run[h] = -INFINITY;
-    l_w[h] = 0.f;
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) o_w[h][d] = 0.f;
-  }
-  __syncthreads();  // barrier init visible before anyone waits
-
-  bool ok = true;
-  // Scores of every staged slot (both sub-chunks) first, then one softmax over the slice and one
-  // pass over V: the slice is at most 128 slots, so no running rescale is needed.
-  // The sub-chunk loops stay rolled: this code runs once per CTA, so its instruction fetches miss
-  // the instruction cache; a smaller body is faster than an unrolled one here.
-  float sc[SLOTS][ROUNDS];
-#pragma unroll 1
-  for (int j = 0; j < SLOTS; ++j) {
-#pragma unroll
-    for (int r = 0; r < ROUNDS; ++r) sc[j][r] = -INFINITY;
-    if (j < n_sub) {  // CTA-uniform
-      if (!mbar_wait(&bar[j], (!reuse && j < hsub) ? 1 : 0, a.status)) ok = false;
-      if (!__all_sync(0xffffffffu, ok)) ok = false;
-      if (j == 0 && threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 2);
-      const __half* Kj = Ks + (size_t)j * kAttnSub * HD;
-      float* Sj = S + j * GQ * kAttnSub;
-      const int cn = min(kAttnSub, n - j * kAttnSub);
-      if (reuse && a.step) {
-        const int c0 = t0 + j * kAttnSub;
-        if ((kv_pos >= c0 && kv_pos < c0 + cn) || (kv_sink > 0 && c0 < kv_sink)) {  // CTA-uniform
-          if (patch_row >= c0 && patch_row < c0 + cn)
-            *reinterpret_cast<uint4*>((patch_k ? Ks : Vs) + ((size_t)j * kAttnSub + (patch_row - c0)) * HD + patch_col * 8) = patch;
-          __syncthreads();
-        }
+    for (int kk = 0; kk < KS; ++kk) {
+      float2 x0 = make_float2(0.f, 0.f), x1 = x0;
+      if (gh < GQ) {
+        x0 = __ldcg(reinterpret_cast<const float2*>(qp + 16 * kk));
+        x1 = __ldcg(reinterpret_cast<const float2*>(qp + 16 * kk + 8));
       }
-      // scores for this warp's 8 slots, GQ heads
-#pragma unroll
-      for (int r = 0; r < ROUNDS; ++r) {
-        float part[NV];
-#pragma unroll
-        for (int i = 0; i < PR; ++i) {
-          const int p = warp * 8 + r * PR + i;
-          float kf[DPL];
-          if (p < cn) {
-            if (DPL == 4) {
-              uint2 raw = *reinterpret_cast<const uint2*>(Kj + (size_t)p * HD + lane * 4);
-              float2 a0 = __half22float2(*reinterpret_cast<__half2*>(&raw.x));
-              float2 a1 = __half22float2(*reinterpret_cast<__half2*>(&raw.y));
-              kf[0] = a0.x; kf[1 % DPL] = a0.y; kf[2 % DPL] = a1.x; kf[3 % DPL] = a1.y;
-            } else {
-              float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(Kj + (size_t)p * HD + lane * 2));
-              kf[0] = a0.x; kf[1 % DPL] = a0.y;
-            }
-          } else {
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) kf[d] = 0.f;
-          }
-#pragma unroll
-          for (int h = 0; h < GQ; ++h) {
-            float acc = 0.f;
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) acc = fmaf(qr[h][d], kf[d], acc);
-            part[i * GQ + h] = acc;
-          }
-        }
-        const float tot = warp_reduce_scatter<NV>(part, lane);
-        const int idx = lane >> (5 - LOG_NV);
-        const int p = warp * 8 + r * PR + idx / GQ;
-        const int h = idx % GQ;
-        sc[j][r] = (p < cn) ? tot / rsq : -INFINITY;
-        if ((lane & ((32 >> LOG_NV) - 1)) == 0) Sj[h * kAttnSub + p] = sc[j][r];
-      }
+      split_f16x2(x0.x, x0.y, qh[kk][0], ql[kk][0]);
+      split_f16x2(x1.x, x1.y, qh[kk][1], ql[kk][1]);
     }
   }
+  cp_async_wait<0>();
+  __syncthreads();  // every thread's rows have landed
+  if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 2);
+
+  // this warp's 16 slots: rows 16 warp ..
+  const int my_n = min(16, n - warp * 16);
+  if (my_n > 0)
+    attn_group<HD, GQ, RB>(ks_s, vs_s, warp * 16, my_n, lane, qh, ql, red + warp * GQ * RS, red_m + warp * GQ,
+                           red_l + warp * GQ);
   __syncthreads();
   if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 5);
 
-  // softmax over the slice: every warp derives the same max from all staged scores
+  // CTA max per head, warp weights and the CTA sum (warp 0; lanes in groups of 8 = warps of a head)
+  if (warp == 0) {
 #pragma unroll
-  for (int h = 0; h < GQ; ++h) {
-    float mx = -INFINITY;
+    for (int base = 0; base < 8 * GQ; base += 32) {
+      const int idx = base + lane, h = idx >> 3, w = idx & 7;
+      const bool v = idx < 8 * GQ && w < nw;
+      const float mw = v ? red_m[w * GQ + h] : -INFINITY;
+      float M = mw;
 #pragma unroll
-    for (int j = 0; j < SLOTS; ++j)
-      if (j < n_sub) mx = fmaxf(mx, fmaxf(S[(j * GQ + h) * kAttnSub + lane], S[(j * GQ + h) * kAttnSub + lane + 32]));
-    m_run[h] = warp_max(mx);
-  }
-#pragma unroll 1
-  for (int j = 0; j < SLOTS; ++j) {
-    if (j >= n_sub) break;
-    const __half* Vj = Vs + (size_t)j * kAttnSub * HD;
-    const int cn = min(kAttnSub, n - j * kAttnSub);
-    // probabilities for the slots this lane scored, then broadcast per slot
-    float pv[ROUNDS];
+      for (int off = 1; off < 8; off <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      const float wt = v ? expf(mw - M) : 0.f;
+      float L = v ? wt * red_l[w * GQ + h] : 0.f;
 #pragma unroll
-    for (int r = 0; r < ROUNDS; ++r) {
-      const int idx = lane >> (5 - LOG_NV);
-      const int h = idx % GQ;
-      float mh = m_run[0];
-#pragma unroll
-      for (int hh = 0; hh < GQ; ++hh)
-        if (hh == h) mh = m_run[hh];
-      pv[r] = (sc[j][r] == -INFINITY) ? 0.f : expf(sc[j][r] - mh);
-    }
-#pragma unroll
-    for (int r = 0; r < ROUNDS; ++r) {
-#pragma unroll
-      for (int i = 0; i < PR; ++i) {
-        const int p = warp * 8 + r * PR + i;
-        float vf[DPL];
-        const bool valid = p < cn;
-        if (valid) {
-          if (DPL == 4) {
-            uint2 raw = *reinterpret_cast<const uint2*>(Vj + (size_t)p * HD + lane * 4);
-            float2 a0 = __half22float2(*reinterpret_cast<__half2*>(&raw.x));
-            float2 a1 = __half22float2(*reinterpret_cast<__half2*>(&raw.y));
-            vf[0] = a0.x; vf[1 % DPL] = a0.y; vf[2 % DPL] = a1.x; vf[3 % DPL] = a1.y;
-          } else {
-            float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(Vj + (size_t)p * HD + lane * 2));
-            vf[0] = a0.x; vf[1 % DPL] = a0.y;
-          }
-        }
-#pragma unroll
-        for (int h = 0; h < GQ; ++h) {
-          const float ph = __shfl_sync(0xffffffffu, pv[r], ((i * GQ + h) << (5 - LOG_NV)));
-          if (valid) {
-            l_w[h] += ph;
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) o_w[h][d] = fmaf(ph, vf[d], o_w[h][d]);
-          }
+      for (int off = 1; off < 8; off <<= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (idx < 8 * GQ) {
+        wgt[w * GQ + h] = wt;
+        if (w == 0) {
+          tot[h] = M;
+          tot[GQ + h] = L;
         }
       }
     }
-  }
-
-  if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 6);
-  // combine the 8 warps (identical running max) through shared memory reused from the K stage
-  __syncthreads();
-  float* red = reinterpret_cast<float*>(smem);  // [8][GQ][HD + 1]
-  constexpr int RS = HD + 1;
-#pragma unroll
-  for (int h = 0; h < GQ; ++h) {
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) red[(warp * GQ + h) * RS + lane * DPL + d] = o_w[h][d];
-    if (lane == 0) red[(warp * GQ + h) * RS + HD] = l_w[h];
   }
   __syncthreads();
   const bool single = (n_act == 1);
-  for (int e = threadIdx.x; e < GQ * (HD + 1); e += kAttnThreads) {
-    const int h = e / (HD + 1), d = e % (HD + 1);
-    float s = 0.f;
+  for (int e = threadIdx.x; e < GQ * HD; e += kAttnThreads) {
+    const int h = e / HD, d = e % HD;
+    float O = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += red[(w * GQ + h) * RS + d];
+    for (int w = 0; w < 8; ++w)
+      if (w < nw) O = fmaf(wgt[w * GQ + h], red[(w * GQ + h) * RS + d], O);
     const int hq = g * GQ + h;
     if (single) {
-      if (d < HD) {
-        float l = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) l += red[(w * GQ + h) * RS + HD];
-        a.out[(size_t)hq * HD + d] = s / l;
-      }
+      a.out[(size_t)hq * HD + d] = O / tot[GQ + h];
     } else {
       float* pp = a.part + ((size_t)hq * s_max + sidx) * PS;
-      pp[d == HD ? HD + 1 : d] = s;  // o[0..HD), l at HD+1
-      if (d == 0) pp[HD] = m_run[h];
+      pp[d] = O;  // o[0..HD), m at HD, l at HD + 1
+      if (d == 0) {
+        pp[HD] = tot[h];
+        pp[HD + 1] = tot[GQ + h];
+      }
     }
   }
   if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 3);
-  if (single || !ok) {
+  if (single) {
     if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 4);
     return;
   }
 
-  // last-arriving slice of this kv head merges all slices
+  // last-arriving slice of this kv head merges all slices (the merge's bulk copy reuses the rows'
+  // shared memory: order the earlier writes to it before the async proxy)
+  fence_proxy_async_smem();
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -478,15 +446,10 @@ AttnPlan attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len) {
   if (!p.fn) return p;
   p.s_max = (max_seq_len + kAttnCapacity - 1) / kAttnCapacity;
   p.grid = dim3(p.s_max, n_kv_heads);
-  const size_t kv = attn_stage_bytes(head_dim);  // K,V x 2 sub-chunk slots
-  const size_t sc = (size_t)2 * gq * kAttnSub * 4;
-  const size_t red = (size_t)8 * gq * (head_dim + 1) * 4;
-  // the combine buffer and the merge reuse the K/V stage region (red <= kv for every instantiated
-  // HD, GQ; the region grows to the merge records when they are larger and fit)
-  p.smem = attn_region_bytes(head_dim, gq, p.s_max) + sc + 2 * 8 + 8;
-  if (red > kv) return p;
+  // the rows / merge region, the warp-combine buffer, 3 barriers
+  p.smem = attn_region_bytes(head_dim, gq, p.s_max) + (attn_red_bytes(head_dim, gq) + 15) / 16 * 16 + 3 * 8;
   p.part_floats = (size_t)n_heads * p.s_max * attn_part_stride(head_dim);
-  p.ok = p.smem <= 226 * 1024;
+  p.ok = p.smem <= 226 * 1024;  // two CTAs per SM up to 113 KB
   return p;
 }
 

@@ -8,7 +8,7 @@
 
 namespace yb {
 
-constexpr int kAttnCapacity = 128;  // cache slots one CTA covers (two staged sub-chunks of 64)
+constexpr int kAttnCapacity = 128;  // cache slots one CTA covers (8 warps x 16)
 
 struct AttnArgs {
   const float* q;         // [n_heads][head_dim]
@@ -22,9 +22,9 @@ struct AttnArgs {
   int max_seq_len;
   unsigned* status;
   // optional timeline (null = off): per CTA c = blockIdx.y * gridDim.x + blockIdx.x,
-  // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 1 inputs ready, 2 first K/V
-  // sub-chunk staged, 5 scores done, 6 V pass done (thread 0), 3 slice partial written, 4 exit
-  // (inactive slices stamp only 0 and 1)
+  // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 1 inputs ready, 2 K/V rows staged,
+  // 5 slot groups done (thread 0), 3 slice partial written, 4 exit (inactive slices stamp only 0
+  // and 1)
   unsigned long long* trace;
   int trace_stride;
 };
@@ -38,10 +38,13 @@ struct AttnPlan {
   size_t part_floats;
 };
 
-// Shared memory of one attention CTA before the score buffer: the K/V stage, or, when larger and
-// below kAttnMergeSmemMax, the slice partials of one kv head (merged in shared memory).
+// Shared memory of one attention CTA: a region holding the staged K/V rows, or, when larger and
+// below kAttnMergeSmemMax, the slice partials of one kv head (merged in shared memory); then the
+// warp-combine buffer and the barriers.
 constexpr size_t kAttnMergeSmemMax = 96 * 1024;
-__host__ __device__ constexpr size_t attn_stage_bytes(int hd) { return (size_t)2 * 2 * 64 * hd * 2; }
+// Shared-memory row of a staged cache slot: head_dim fp16 padded by 16 bytes (an odd multiple of 16).
+__host__ __device__ constexpr int attn_row_bytes(int hd) { return hd * 2 + 16; }
+__host__ __device__ constexpr size_t attn_stage_bytes(int hd) { return (size_t)2 * kAttnCapacity * attn_row_bytes(hd); }
 __host__ __device__ constexpr size_t attn_merge_bytes(int hd, int gq, int s_max) {
   return (size_t)gq * s_max * (hd + 4) * 4 + (size_t)2 * gq * s_max * 4;
 }
@@ -52,6 +55,12 @@ __host__ __device__ constexpr size_t attn_region_bytes(int hd, int gq, int s_max
   return attn_merge_in_smem(hd, gq, s_max) && attn_merge_bytes(hd, gq, s_max) > attn_stage_bytes(hd)
              ? (attn_merge_bytes(hd, gq, s_max) + 127) / 128 * 128
              : attn_stage_bytes(hd);
+}
+
+// Warp-combine buffer: per warp and head the output row (head_dim + 4 floats), max and sum, the
+// warp weights, then per head the CTA max and sum.
+__host__ __device__ constexpr size_t attn_red_bytes(int hd, int gq) {
+  return ((size_t)8 * gq * (hd + 4) + (size_t)8 * gq * 3 + (size_t)2 * gq) * 4;
 }
 
 AttnPlan attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
