@@ -165,38 +165,79 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const Attn
     mbar_fence_init();
   }
 
+  const int s_max = gridDim.x;
+  // A cache of at most one CTA's capacity goes to slice 0 alone (no merge); longer ones split into
+  // slices of at least kAttnSub slots. Slice sidx covers [t0, t1); n_act slices are active.
+  auto slice = [s_max, sidx](int len, int& t0_, int& t1_, int& nact_) {
+    int ch = (len + s_max - 1) / s_max;
+    ch = ((ch + 15) / 16) * 16;
+    if (len <= kAttnCapacity) ch = kAttnCapacity;
+    else if (ch < kAttnSub) ch = kAttnSub;
+    nact_ = (len + ch - 1) / ch;
+    t0_ = sidx * ch;
+    t1_ = min(len, t0_ + ch);
+  };
+  // cache rows [r_lo, r_hi) of this kv head to shared rows r - base (K and V)
+  const __half* kg = a.k_cache + (size_t)g * a.max_seq_len * HD;
+  const __half* vg = a.v_cache + (size_t)g * a.max_seq_len * HD;
+  auto stage = [&](int base, int r_lo, int r_hi) {
+    for (int e = threadIdx.x; e < (r_hi - r_lo) * CH; e += kAttnThreads) {
+      const int r = r_lo + e / CH, c = e % CH;
+      const size_t off = (size_t)r * HD + c * 8;
+      cp_async16(ks_s + (r - base) * RB + c * 16, kg + off, 16u);
+      cp_async16(vs_s + (r - base) * RB + c * 16, vg + off, 16u);
+    }
+  };
+
+  // Before the wait on the QKV kernel: stage the rows of this slice that are final already, for
+  // the kv_len the step state shows now (normally this step's, possibly the previous step's: it is
+  // only a hint) -- all but its newest slot (the one this step's QKV kernel may be appending) and,
+  // past the context, the re-rotated sink keys.  The check after the wait keeps them only when they
+  // still fit the slice and hold neither slot the QKV kernel writes.
+  int h0, h1, hact, ps0, ps1;
+  {
+    int hlen = a.step ? *reinterpret_cast<const volatile int*>(&a.step->kv_len) : a.kv_len;
+    const int hsink = a.step ? *reinterpret_cast<const volatile int*>(&a.step->kv_sink) : 0;
+    hlen = hlen < 1 ? 1 : (hlen > a.max_seq_len ? a.max_seq_len : hlen);
+    slice(hlen, h0, h1, hact);
+    ps0 = max(h0, hsink > 0 ? 2 : 0);
+    ps1 = min(h1, hlen - 1);
+    if (ps1 < ps0) ps1 = ps0;
+  }
+  stage(h0, ps0, ps1);
+  cp_async_commit();
+
   pdl_wait();  // q and the newest K/V slot come from the QKV kernel
   if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 1);
 
   const int kv_len = a.step ? a.step->kv_len : a.kv_len;
-  const int s_max = gridDim.x;
-  // A cache of at most one CTA's capacity goes to slice 0 alone (no merge); longer ones split into
-  // slices of at least kAttnSub slots. Slice sidx covers [t0, t1); n_act slices are active.
-  int ch = (kv_len + s_max - 1) / s_max;
-  ch = ((ch + 15) / 16) * 16;
-  if (kv_len <= kAttnCapacity) ch = kAttnCapacity;
-  else if (ch < kAttnSub) ch = kAttnSub;
-  const int n_act = (kv_len + ch - 1) / ch;
-  const int t0 = sidx * ch;
-  const int t1 = min(kv_len, t0 + ch);
-  if (t0 >= kv_len) return;  // inactive slice (not counted by the merge)
+  const int kv_pos = a.step ? a.step->kv_pos : -1;
+  const int kv_sink = a.step ? a.step->kv_sink : 0;
+  int t0, t1, n_act;
+  slice(kv_len, t0, t1, n_act);
+  if (t0 >= kv_len) {  // inactive slice (not counted by the merge): let the early copies land
+    cp_async_wait<0>();
+    return;
+  }
   const int n = t1 - t0;
   const int nw = (n + 15) / 16;  // warps with slots
-
-  // K and V rows [t0, t1) of this kv head; V rows up to the last warp's 16-slot boundary are
-  // zero-filled so 0 * v stays 0 (K rows there are masked out of the softmax)
-  {
-    const __half* kg = a.k_cache + ((size_t)g * a.max_seq_len + t0) * HD;
-    const __half* vg = a.v_cache + ((size_t)g * a.max_seq_len + t0) * HD;
-    for (int e = threadIdx.x; e < nw * 16 * CH; e += kAttnThreads) {
-      const int r = e / CH, c = e % CH;
-      const bool in = r < n;
-      const size_t off = in ? (size_t)r * HD + c * 8 : 0;
-      if (in) cp_async16(ks_s + r * RB + c * 16, kg + off, 16u);
-      cp_async16(vs_s + r * RB + c * 16, vg + off, in ? 16u : 0u);
+  const bool keep = ps1 > ps0 && t0 == h0 && ps1 <= t1 && !(kv_pos >= ps0 && kv_pos < ps1) && ps0 >= kv_sink;
+  if (!keep) {
+    if (ps1 > ps0) {  // the early copies land before their rows are written again
+      cp_async_wait<0>();
+      __syncthreads();
     }
-    cp_async_commit();
+    ps0 = ps1 = t0;
   }
+  // the rest of [t0, t1); V rows up to the last warp's 16-slot boundary are zero-filled so
+  // 0 * v stays 0 (K rows there are masked out of the softmax)
+  stage(t0, t0, ps0);
+  stage(t0, ps1, t1);
+  for (int e = threadIdx.x; e < (nw * 16 - n) * CH; e += kAttnThreads) {
+    const int r = n + e / CH, c = e % CH;
+    cp_async16(vs_s + r * RB + c * 16, vg, 0u);
+  }
+  cp_async_commit();
 
   // q of the GQ heads as the B operand of the score mma: lane (gh = lane / 4, c4 = lane % 4) holds
   // head gh, dims 16 kk + 2 c4 (+1) and 16 kk + 8 + 2 c4 (+1), as hi and lo fp16 pairs
