@@ -319,20 +319,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const Attn
 
   // last-arriving slice of this kv head merges all slices (the merge's bulk copy reuses the rows'
   // shared memory: order the earlier writes to it before the async proxy)
+  // The counter's release (by thread 0, after the barrier) publishes this CTA's partial record; the
+  // last arrival's acquire makes every slice's record visible to the reads below.
   fence_proxy_async_smem();
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&a.counters[g], 1u);
+    const unsigned prev = atom_add_acq_rel_gpu(&a.counters[g], 1u);
     s_last = (prev == (unsigned)(n_act - 1));
   }
-  __syncthreads();
+  __syncthreads();  // also: the combine buffer is no longer read (smem reuse below)
   if (!s_last) {
     if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 4);
     return;
   }
-  __threadfence();
-  __syncthreads();  // smem reuse: the combine buffer is no longer read
   if (merge_smem) {
     // Merge (log-sum-exp) in shared memory: one bulk copy per head brings every slice's
     // (o, m, l) record; slice weights exp(m_s - M) and the outputs are then formed from there.

@@ -188,6 +188,14 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 // one thread after a CTA barrier, it publishes every write the CTA made before the barrier (the
 // release is cumulative over writes ordered before it by the barrier), so only that thread pays
 // for the system-scope fence.
+// Counter add with acquire-release semantics at GPU scope; returns the previous value.  After a
+// __syncthreads, one thread's release publishes the whole CTA's earlier writes (release is
+// cumulative over what the barrier ordered before it); the acquire orders the caller's later reads.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
