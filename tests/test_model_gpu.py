@@ -119,6 +119,26 @@ def test_ring_buffer_and_sinks_vs_reference(gpu, tiny_yalm, executor):
     m.close()
 
 
+@pytest.mark.parametrize("executor", ["persistent", "graph"])
+def test_context_growth_and_restart_vs_reference(gpu, tiny_yalm, executor):
+    """Context 256: positions 0-127 fit one attention CTA (the graph executor replays its one-slice
+    attention graph there), 128-255 split the cache over two slices with the log-sum-exp merge,
+    256-299 wrap the ring with sinks; then a new sequence restarts at position 0, so the first
+    steps see the previous sequence's cache length in the step state until they overwrite it."""
+    m = _make(tiny_yalm, executor, context=256)
+    ref = oracle.RefModel(tiny_yalm, context=256)
+    s = InferenceState(m.config)
+    rng = np.random.default_rng(11)
+    toks = rng.integers(0, m.config.vocab_size, 312)
+    for i, tok in enumerate(toks):
+        pos = i if i < 300 else i - 300
+        m.forward(s, int(tok), pos)
+        exp = ref.forward(int(tok), pos, 1)
+        got = s.logits()
+        assert np.abs(got - exp).max() <= LOGIT_MAX_ABS and _cos(got, exp) >= LOGIT_COS, (i, pos)
+    m.close()
+
+
 def test_errors_are_returned_not_aborted(tiny_model):
     from yalm_b200 import YalmB200Error
     s = InferenceState(tiny_model.config)
