@@ -174,9 +174,6 @@ __device__ __forceinline__ void split_f16x2(float x, float y, uint32_t& hi, uint
   hi = *reinterpret_cast<const uint32_t*>(&h);
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
-// Byte offset of 16-byte chunk c (0..7) of row r in a box of 128-byte rows written by TMA with
-// CU_TENSOR_MAP_SWIZZLE_128B (box base 1024-byte aligned).
-__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 // ---------------------------------------------------------------- system-scope flags (peer memory)
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
