@@ -1,7 +1,8 @@
 """Isolated decode-kernel benchmark (benchmark config 4; the counterpart of yalm's
 `build/test -bk {matmul,matmul-wide,mha,ffn}`, src/test.cpp:339-405).
 
-    python -m yalm_b200.kbench [--kernel gemv|gateup|qkv|attention|all] [--iters N] [--quick]
+    python -m yalm_b200.kbench [--kernel gemv|gateup|qkv|attention|prefill_attention|prefill|all]
+                               [--iters N] [--warm W] [--quick]
 
 Each launch goes through the C ABI (yb_gemv_dev, yb_gateup_dev, yb_qkv_dev, yb_attention_dev) on
 seeded inputs: W ~ N(0, 0.02) fp16, x ~ N(0, 1), q/K/V ~ N(0, 1) fp16.  Launches rotate over enough
@@ -32,9 +33,12 @@ def _copies(nbytes):
     return max(1, math.ceil(4 * L2_BYTES / nbytes))
 
 
-def _time(fn, iters, warm=3):
+_WARM = 3
+
+
+def _time(fn, iters, warm=None):
     import torch
-    for i in range(warm):
+    for i in range(_WARM if warm is None else warm):
         fn(i)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -139,15 +143,56 @@ def bench_prefill_attention(nh, nkv, hd, T, iters, seed=0):
             "us": round(ms * 1000, 2), "tflops": round(flop / (ms / 1000) / 1e12, 1)}
 
 
+def bench_prefill(tokens, iters, config="mistral-7b", seed=0):
+    """The whole batched prompt pass (yb_prefill, every layer's GEMMs, norms, RoPE / KV append and
+    attention, then the classifier) of the seeded synthetic checkpoint.  Per prompt length one
+    untimed call sizes the buffers and loads the kernels; then `iters` calls are timed, each by
+    wall clock around the call and a yb_sync."""
+    import os
+    import time
+    from . import synth
+    from .codec import YALMData
+    from .model import Model
+    shape = synth.shape_with(config)
+    path = os.path.join(synth.scratch_dir(synth.file_bytes(shape)), f"yalm_{config}_seed0.yalm")
+    synth.write_yalm(path, shape, seed=0)
+    m = Model(YALMData(path)).cuda(0)
+    rng = np.random.default_rng(seed)
+    rows = []
+    try:
+        for t in tokens:
+            prompt = rng.integers(0, m.config.vocab_size, t)
+            m.prefill(prompt, 0)
+            m.sync()
+            best = total = 0.0
+            for i in range(iters):
+                t0 = time.perf_counter()
+                m.prefill(prompt, 0)
+                m.sync()
+                dt = time.perf_counter() - t0
+                total += dt
+                best = dt if i == 0 else min(best, dt)
+            rows.append({"kernel": "prefill", "config": config, "tokens": t, "iters": iters,
+                         "mean_s": round(total / iters, 4), "best_s": round(best, 4),
+                         "tok_s": round(t * iters / total, 1)})
+    finally:
+        m.close()
+    return rows
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", default="all", choices=["gemv", "gateup", "qkv", "attention", "prefill_attention", "all"])
+    ap.add_argument("--kernel", default="all",
+                    choices=["gemv", "gateup", "qkv", "attention", "prefill_attention", "prefill", "all"])
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--quick", action="store_true", help="one shape per kernel (for profiler captures)")
     ap.add_argument("--kv-lens", default="", help="attention: comma-separated kv_len values")
     ap.add_argument("--msl", type=int, default=0, help="attention: cache capacity (default: kv_len)")
-    ap.add_argument("--tokens", default="", help="prefill_attention: comma-separated prompt lengths")
+    ap.add_argument("--tokens", default="", help="prefill_attention, prefill: comma-separated prompt lengths")
+    ap.add_argument("--warm", type=int, default=3, help="untimed launches per case before the timed ones")
     args = ap.parse_args(argv)
+    global _WARM
+    _WARM = args.warm
     import torch
     torch.cuda.set_device(0)
     rows = []
@@ -169,6 +214,9 @@ def main(argv=None):
         lens = [int(v) for v in args.tokens.split(",")] if args.tokens else ([1024] if args.quick else [1024, 3202])
         for t in lens:
             rows.append(bench_prefill_attention(32, 8, 128, t, max(3, args.iters // 20)))
+    if args.kernel == "prefill":  # not part of "all": it writes and loads the 14 GB 7B checkpoint
+        lens = [int(v) for v in args.tokens.split(",")] if args.tokens else [3202, 1024]
+        rows.extend(bench_prefill(lens, max(1, args.iters // 100)))
     for r in rows:
         print(json.dumps(r))
 
