@@ -87,6 +87,36 @@ def test_restatement_vs_reference_tiny(tiny_yalm):
         assert np.abs(oracle.h2f(v1) - oracle.h2f(v2)).max() < 5e-3
 
 
+def test_restatement_vs_reference_gqa4_ring(tmp_path):
+    """A second architecture (head_dim 128, 4 query heads per kv head, 2 layers) opened with a
+    32-slot context and run to position 80: whole steps past the context, where yalm's CPU path
+    writes the ring and re-rotates the sink keys (src/infer.cpp:296-325), agree between the C
+    restatement and yalm's own code."""
+    from yalm_b200 import synth
+    shape = synth.shape_with("tiny", dim=1024, n_heads=8, n_kv_heads=2, head_dim=128, hidden_dim=2048,
+                             n_layers=2, vocab_size=1024)
+    path = synth.write_yalm(str(tmp_path / "gqa4.yalm"), shape, seed=11)
+    ctx = 32
+    y = YALMData(path)
+    c = Config.from_yalm(y, context=ctx)
+    assert c.max_seq_len == ctx and c.n_heads // c.n_kv_heads == 4 and c.head_dim == 128
+    ref = oracle.RefModel(path, context=ctx)
+    cm = oracle.CModel(y, c)
+    rng = np.random.default_rng(17)
+    toks = rng.integers(0, c.vocab_size, 80)
+    for pos, t in enumerate(toks):
+        a = ref.forward(int(t), pos, 1)
+        b = cm.forward(int(t), pos, 1)
+        assert np.abs(a - b).max() < 2e-3, pos
+        assert float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b))) > 0.99999, pos
+    for l in range(c.n_layers):
+        for h in range(c.n_kv_heads):
+            k1, v1 = ref.read_kv(l, h, 0, ctx)
+            k2, v2 = cm.read_kv(l, h, 0, ctx)
+            assert np.abs(oracle.h2f(k1) - oracle.h2f(k2)).max() < 5e-3
+            assert np.abs(oracle.h2f(v1) - oracle.h2f(v2)).max() < 5e-3
+
+
 def test_restatement_vs_golden(tiny_yalm, golden):
     """The C restatement replays the golden run (generated by yalm's own CPU path)."""
     y = YALMData(tiny_yalm)
