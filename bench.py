@@ -73,6 +73,19 @@ def measured_peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def workload_name(config: str) -> str:
+    """The workload both arms name in their `config` (the reference arm times a bounded sample of it)."""
+    return (f"{config} batch-1 decode: {PROMPT_LEN}-token prompt, decode positions "
+            f"{PROMPT_LEN}..{PROMPT_LEN + DECODE_LEN - 1}")
+
+
+def context_of(config: str) -> int:
+    """The context each config's checkpoint is opened with: yalm caps max_seq_len at 4096 unless a
+    context is given (src/model.cpp:30-34); the 70B config asks for 8192."""
+    from yalm_b200 import synth
+    return 8192 if config == "llama-70b" else min(4096, synth.SHAPES[config].max_seq_len)
+
+
 def model_file(config: str, rank: int, world: int, dist, dtype: str = "fp16"):
     from yalm_b200 import synth
     shape = synth.shape_with(config, dtype=dtype)
@@ -184,8 +197,9 @@ def run_reference(args):
         "steps": len(steps), "warmup": args.warmup, "ms_per_step": round(1000 * t / len(steps), 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 weights, f32 compute",
         "data": "synthetic (seeded N(0,0.02) fp16 weights, random token ids)",
-        "config": {"workload": f"{args.config} batch-1 decode, yalm CPU path", "model": args.config,
-                   "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_LEN, "parallelism": "cpu"},
+        "config": {"workload": workload_name(args.config), "model": args.config, "global_batch": 1,
+                   "seq_len": PROMPT_LEN + DECODE_LEN, "context": context_of(args.config),
+                   "parallelism": "cpu (yalm -d cpu, OpenMP)"},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
                          "sample": sample},
@@ -419,8 +433,7 @@ def main():
             "scaling": "strong", "vs_baseline": None,
             "dtype": ("f16" if args.dtype == "fp16" else "f8e5m2") + " weights, f32 accumulate/activations",
             "data": "synthetic (seeded N(0,0.02) fp16 weights in the .yalm layout, random token ids)",
-            "config": {"workload": f"{args.config} batch-1 decode: {PROMPT_LEN}-token prompt, decode positions "
-                                   f"{PROMPT_LEN}..{PROMPT_LEN + DECODE_LEN - 1}", "model": args.config,
+            "config": {"workload": workload_name(args.config), "model": args.config,
                        "global_batch": 1, "seq_len": PROMPT_LEN + DECODE_LEN, "context": c.max_seq_len,
                        "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights streamed every step: "
                                                           f"{step_bytes / 1e9:.2f} GB/step/rank)"},
