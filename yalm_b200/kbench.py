@@ -7,9 +7,10 @@
 Each launch goes through the C ABI (yb_gemv_dev, yb_gateup_dev, yb_qkv_dev, yb_attention_dev) on
 seeded inputs: W ~ N(0, 0.02) fp16, x ~ N(0, 1), q/K/V ~ N(0, 1) fp16.  Launches rotate over enough
 distinct weight / cache copies to cover at least 4x the 126 MB L2, so every launch streams from HBM.
-Time is measured with CUDA events around `iters` back-to-back launches on one stream; GB/s counts
-algorithmic bytes (weights + activations in/out; for attention K + V + q + out).  Prints one JSON
-line per case.
+Time is measured with CUDA events around `iters` back-to-back launches on one stream (the mean; a
+second pass with an event after every launch gives the per-launch p10 / p50 / p90, which include
+that event's drain); GB/s counts algorithmic bytes (weights + activations in/out; for attention
+K + V + q + out).  Prints one JSON line per case.
 """
 from __future__ import annotations
 
@@ -36,18 +37,40 @@ def _copies(nbytes):
 _WARM = 3
 
 
+_LAST_SPREAD: dict = {}
+
+
 def _time(fn, iters, warm=None):
+    """Mean milliseconds per launch over `iters` back-to-back launches, and (kept in _LAST_SPREAD for
+    the caller's JSON line) the per-launch p10 / p50 / p90 in microseconds from a second pass with an
+    event recorded after every launch.  An event makes the stream drain the kernel before the next
+    one starts, so the spread pass reads 1-3 us per launch above the mean pass for the short kernels;
+    the mean is the throughput figure.  Both passes queue their launches behind a device-side spin
+    (~30 us of SM cycles per launch), so host launch overhead enters neither."""
     import torch
     for i in range(_WARM if warm is None else warm):
         fn(i)
     torch.cuda.synchronize()
+    spin = 60_000 * max(1, iters)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(spin)
     a.record()
     for i in range(iters):
         fn(i)
     b.record()
     b.synchronize()
-    return a.elapsed_time(b) / iters
+    mean_ms = a.elapsed_time(b) / iters
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(iters + 1)]
+    torch.cuda._sleep(spin)
+    ev[0].record()
+    for i in range(iters):
+        fn(i)
+        ev[i + 1].record()
+    ev[-1].synchronize()
+    per = np.array([ev[i].elapsed_time(ev[i + 1]) for i in range(iters)]) * 1000.0
+    _LAST_SPREAD.clear()
+    _LAST_SPREAD.update({f"p{q}_us": round(float(np.percentile(per, q)), 2) for q in (10, 50, 90)})
+    return mean_ms
 
 
 def bench_gemv(rows, cols, iters, kind="gemv", seed=0):
@@ -74,7 +97,7 @@ def bench_gemv(rows, cols, iters, kind="gemv", seed=0):
     ms = _time(fn, iters)
     nbytes = wbytes + cols * 4 + ybytes
     return {"kernel": kind, "rows": rows, "cols": cols, "us": round(ms * 1000, 2),
-            "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
+            "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n, **_LAST_SPREAD}
 
 
 def bench_qkv(dim, nh, nkv, hd, msl, iters, seed=0):
@@ -99,7 +122,7 @@ def bench_qkv(dim, nh, nkv, hd, msl, iters, seed=0):
     ms = _time(fn, iters)
     nbytes = wbytes + dim * 8 + nh * hd * 4 + 2 * nkv * hd * 2
     return {"kernel": "qkv+rope+kv_append", "rows": rows, "cols": dim, "us": round(ms * 1000, 2),
-            "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
+            "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n, **_LAST_SPREAD}
 
 
 def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
@@ -121,7 +144,7 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
     ms = _time(fn, iters)
     nbytes = kvbytes + 2 * nh * hd * 4
     return {"kernel": "attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "kv_len": kv_len, "max_seq_len": msl,
-            "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n}
+            "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n, **_LAST_SPREAD}
 
 
 def bench_prefill_attention(nh, nkv, hd, T, iters, seed=0):
@@ -140,7 +163,7 @@ def bench_prefill_attention(nh, nkv, hd, T, iters, seed=0):
     ms = _time(fn, iters)
     flop = 4.0 * nh * hd * T * (T + 1) / 2  # q.k and p.v over the causal triangle
     return {"kernel": "prefill_attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "tokens": T,
-            "us": round(ms * 1000, 2), "tflops": round(flop / (ms / 1000) / 1e12, 1)}
+            "us": round(ms * 1000, 2), "tflops": round(flop / (ms / 1000) / 1e12, 1), **_LAST_SPREAD}
 
 
 def bench_prefill(tokens, iters, config="mistral-7b", seed=0):
