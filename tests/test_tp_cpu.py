@@ -1,4 +1,4 @@
-"""The tensor-parallel partition on CPU ranks (gloo, world size 2): each rank runs the decode math
+"""The tensor-parallel partition on CPU ranks (gloo, world sizes 2 and 4): each rank runs the decode math
 of its shard (yalm_b200.tp.shard — the slices the engine uploads), the wo / w2 partial sums are
 exchanged and added in rank order as the engine's kernels do, the logits are gathered, and the
 result must equal the unsharded forward pass."""
@@ -102,12 +102,14 @@ def _rank_main(rank, world, port, path, toks, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_tensor_parallel_partition_gloo(tiny_yalm, world):
+@pytest.mark.parametrize("world,kv_heads", [(2, 2), (4, 4)])
+def test_tensor_parallel_partition_gloo(tiny_yalm, world, kv_heads):
     import torch.multiprocessing as mp
     from yalm_b200 import Config, YALMData, synth
-    # a 2-layer slice of the tiny architecture keeps the numpy reference fast
-    path = synth.write_yalm(tiny_yalm.replace(".yalm", "_2l.yalm"), synth.shape_with("tiny", n_layers=2), seed=0)
+    # a 2-layer slice of the tiny architecture keeps the numpy reference fast; 4 ranks need 4 kv
+    # heads (each GQA group stays whole on one rank)
+    path = synth.write_yalm(tiny_yalm.replace(".yalm", f"_2l_kv{kv_heads}.yalm"),
+                            synth.shape_with("tiny", n_layers=2, n_kv_heads=kv_heads), seed=0)
     toks = [5, 77, 1200, 3]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -126,3 +128,33 @@ def test_tensor_parallel_partition_gloo(tiny_yalm, world):
         assert np.array_equal(res[r], res[0])  # every rank holds identical logits
     # fp32 reassociation of the split dot products only
     assert np.abs(res[0] - full).max() < 2e-4
+
+
+def test_partition_covers_every_row_once_and_rejects_uneven_worlds():
+    """The slices of all ranks tile Wq / Wk / Wv / W1 / W3 / classifier rows exactly once, in rank
+    order; a world size that would split a GQA group or the hidden units unevenly is refused."""
+    from yalm_b200 import synth
+    from yalm_b200.tp import shard
+
+    class C:
+        pass
+    for name in ("mistral-7b", "llama-70b"):
+        shp = synth.SHAPES[name]
+        c = C()
+        c.n_heads, c.n_kv_heads, c.head_dim = shp.n_heads, shp.n_kv_heads, shp.head_dim
+        c.hidden_dim, c.vocab_size = shp.hidden_dim, shp.vocab_size
+        for world in (1, 2, 4, 8):
+            parts = [shard(c, r, world) for r in range(world)]
+            for field, total in (("q_rows", c.n_heads * c.head_dim), ("kv_rows", c.n_kv_heads * c.head_dim),
+                                 ("hidden", c.hidden_dim), ("vocab", c.vocab_size)):
+                sl = [getattr(p, field) for p in parts]
+                assert sl[0].start == 0 and sl[-1].stop == total
+                assert all(a.stop == b.start for a, b in zip(sl, sl[1:]))
+            # the q heads of a rank are exactly the GQA groups of its kv heads
+            gq = c.n_heads // c.n_kv_heads
+            for p in parts:
+                assert p.q_rows.start == p.kv_rows.start * gq and p.q_rows.stop == p.kv_rows.stop * gq
+        with pytest.raises(ValueError):
+            shard(c, 0, 16)  # 8 kv heads cannot go to 16 ranks
+        with pytest.raises(ValueError):
+            shard(c, 0, 3)
