@@ -1,5 +1,6 @@
 """CPU-side checks of the drop-in boundary: the C-ABI library loads without a GPU, exports every
-function include/yalm_b200.h declares, and rejects bad configurations before touching CUDA."""
+function include/yalm_b200.h declares, and rejects bad configurations, NULL handles and impossible
+shapes with error codes before touching CUDA."""
 import ctypes
 import subprocess
 
@@ -96,3 +97,83 @@ def test_synth_is_deterministic(tmp_path):
     y = YALMData(a)
     w = y.tensors["model.layers.0.mlp.w1.weight"].array(y).view("float16").astype("float64")
     assert abs(w.std() - 0.02) < 0.001 and abs(w.mean()) < 0.001
+
+
+def test_null_engine_is_an_error_not_a_crash():
+    """Every entry point that takes an engine handle returns YB_E_INVALID for NULL (yalm would
+    dereference a null Model and crash); the query functions return their neutral value."""
+    L = _lib.lib()
+    out_i, out_f = ctypes.c_int(), ctypes.c_float()
+    toks = (ctypes.c_int * 2)(1, 2)
+    calls = {
+        "yb_forward": lambda: L.yb_forward(None, 1, 0, 1, None),
+        "yb_forward_async": lambda: L.yb_forward_async(None, 1, 0, 0),
+        "yb_forward_sample": lambda: L.yb_forward_sample(None, 1, 0, 0.0, 0.0, ctypes.byref(out_i)),
+        "yb_forward_prob": lambda: L.yb_forward_prob(None, 1, 0, 1, ctypes.byref(out_f)),
+        "yb_prefill": lambda: L.yb_prefill(None, toks, 2, 0, None),
+        "yb_sync": lambda: L.yb_sync(None),
+        "yb_read_kv": lambda: L.yb_read_kv(None, 0, 0, 0, 1, None, None),
+        "yb_clear_status": lambda: L.yb_clear_status(None),
+        "yb_tp_export": lambda: L.yb_tp_export(None, None, 0, None),
+        "yb_tp_import": lambda: L.yb_tp_import(None, None, 0),
+        "yb_profile_kernel": lambda: L.yb_profile_kernel(None, 0, 1, ctypes.byref(out_f)),
+    }
+    for name, call in calls.items():
+        assert call() == _lib.YB_E_INVALID, name
+        assert _lib.last_error(), name
+    assert L.yb_logits_dev(None) is None
+    assert L.yb_stream(None) is None
+    assert L.yb_status(None) == 0
+    assert L.yb_executor(None) == 0
+    L.yb_destroy(None)  # a no-op
+
+
+def test_kernel_entry_points_check_arguments_before_cuda():
+    """The device-pointer and test-hook entry points reject NULL buffers and impossible shapes with
+    YB_E_INVALID before any CUDA call (so without a GPU too); a dummy non-NULL address is never
+    dereferenced on these paths."""
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)
+    bad = {
+        "gemv null y": lambda: L.yb_gemv_dev(None, p, p, 8, 8, None, 0.0, 0, None),
+        "gemv cols % 8": lambda: L.yb_gemv_dev(p, p, p, 8, 12, None, 0.0, 0, None),
+        "gemv rows 0": lambda: L.yb_gemv_dev(p, p, p, 0, 8, None, 0.0, 0, None),
+        "gateup null w": lambda: L.yb_gateup_dev(p, p, None, 8, 8, None, 0.0, 1, None),
+        "gateup dim % 8": lambda: L.yb_gateup_dev(p, p, p, 8, 20, None, 0.0, 1, None),
+        "qkv odd head_dim": lambda: L.yb_qkv_dev(p, p, p, p, p, p, 1e-5, 64, 2, 1, 31, 30, 16, 0, 0, 0, 3e38, p, None),
+        "qkv rotary > head_dim": lambda: L.yb_qkv_dev(p, p, p, p, p, p, 1e-5, 64, 2, 1, 32, 34, 16, 0, 0, 0, 3e38, p, None),
+        "qkv kv_pos past the cache": lambda: L.yb_qkv_dev(p, p, p, p, p, p, 1e-5, 64, 2, 1, 32, 32, 16, 16, 16, 0, 3e38, p, None),
+        "qkv sink past kv_pos": lambda: L.yb_qkv_dev(p, p, p, p, p, p, 1e-5, 64, 2, 1, 32, 32, 16, 3, 3, 4, 3e38, p, None),
+        "qkv null inv_freq": lambda: L.yb_qkv_dev(p, p, p, p, p, p, 1e-5, 64, 2, 1, 32, 32, 16, 0, 0, 0, 3e38, None, None),
+        "attention kv_len 0": lambda: L.yb_attention_dev(p, p, p, p, 8, 2, 64, 128, 0, p, None),
+        "attention kv_len > cache": lambda: L.yb_attention_dev(p, p, p, p, 8, 2, 64, 128, 129, p, None),
+        "attention null scratch": lambda: L.yb_attention_dev(p, p, p, p, 8, 2, 64, 128, 64, None, None),
+        "noalloc null q": lambda: L.yb_attention_dev_noalloc(p, None, p, p, 8, 2, 64, 128, 64, None),
+        "noalloc kv_len > cache": lambda: L.yb_attention_dev_noalloc(p, p, p, p, 8, 2, 64, 128, 200, None),
+        "matmul n % 8": lambda: L.yb_matmul(p, p, p, 12, 4),
+        "mha null k": lambda: L.yb_mha(p, None, None, p, p, 64, 4, 8, 8, 2),
+        "ffn hidden % 8": lambda: L.yb_ffn(p, p, p, p, p, 12, 8, 1),
+        "prefill attention null out": lambda: L.yb_prefill_attention_dev(None, p, p, p, 8, 0, 8, 2, 64, 64, None),
+        "prefill gemm bad epilogue": lambda: L.yb_prefill_gemm_dev(p, None, p, p, 128, 256, 64, 99, 256, None),
+    }
+    for name, call in bad.items():
+        assert call() == _lib.YB_E_INVALID, name
+        assert _lib.last_error(), name
+
+
+def test_noalloc_attention_size_limit_checked_on_the_host():
+    """The allocation-free attention rejects a shape whose scratch exceeds its fixed device array
+    before touching the GPU, naming both sizes; the limit is the header's constant."""
+    L = _lib.lib()
+    limit = 4 << 20
+    p = ctypes.c_void_p(16)
+    # 32 heads of 128 at a 64k-slot cache need more than 4 MiB of slice records
+    assert L.yb_attention_scratch_bytes(32, 8, 128, 65536) > limit
+    assert L.yb_attention_scratch_bytes(32, 8, 128, 4096) <= limit
+    rc = L.yb_attention_dev_noalloc(p, p, p, p, 32, 8, 128, 65536, 100, None)
+    assert rc == _lib.YB_E_INVALID
+    msg = _lib.last_error()
+    assert "exceeds" in msg and str(limit) in msg
+    assert str(L.yb_attention_scratch_bytes(32, 8, 128, 65536)) in msg  # the size the shape needs
+    src = open(_lib.HEADER).read()
+    assert "#define YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)" in src
