@@ -117,6 +117,25 @@ def test_restatement_vs_reference_gqa4_ring(tmp_path):
             assert np.abs(oracle.h2f(v1) - oracle.h2f(v2)).max() < 5e-3
 
 
+def test_restatement_vs_reference_gelu(tmp_path):
+    """The GELU activation (yalm's default act_type, src/model.cpp:41-48; tanh form in its FFN)
+    on a 2-layer tiny checkpoint: whole steps of the C restatement against yalm's CPU path."""
+    from yalm_b200 import synth
+    path = synth.write_yalm(str(tmp_path / "gelu.yalm"), synth.shape_with("tiny", n_layers=2, act_type="gelu"),
+                            seed=13)
+    y = YALMData(path)
+    c = Config.from_yalm(y)
+    assert int(c.act) == 0  # GELU
+    ref = oracle.RefModel(path)
+    cm = oracle.CModel(y, c)
+    rng = np.random.default_rng(19)
+    for pos, t in enumerate(rng.integers(0, c.vocab_size, 16)):
+        a = ref.forward(int(t), pos, 1)
+        b = cm.forward(int(t), pos, 1)
+        assert np.abs(a - b).max() < 2e-3, pos
+        assert float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b))) > 0.99999, pos
+
+
 def test_restatement_vs_golden(tiny_yalm, golden):
     """The C restatement replays the golden run (generated by yalm's own CPU path)."""
     y = YALMData(tiny_yalm)
