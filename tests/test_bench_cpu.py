@@ -1,0 +1,42 @@
+"""Host logic of bench.py without a GPU: the clock record taken during the timed region (median SM
+clock, throttle reasons that make a run invalid) and the workload both arms name."""
+import bench
+
+
+def _line(sm, mx, hw="Not Active", hw_th="Not Active", sw_th="Not Active", cap="Not Active"):
+    active = "0x0000000000000004" if cap == "Active" else "0x0000000000000000"
+    return f"0, {sm}, {mx}, 812.40, {active}, {hw}, {hw_th}, {sw_th}, {cap}"
+
+
+def _summary(lines):
+    s = bench.ClockSampler(0)
+    s.lines = lines
+    return s.summary()
+
+
+def test_clock_summary_median_and_reasons():
+    lines = [_line(1965, 1965), _line(1777, 1965, cap="Active"), _line(1800, 1965, cap="Active"),
+             "garbage line", _line("[N/A]", 1965)]
+    s = _summary(lines)
+    assert s["samples"] == 3 and s["sm_mhz"] == 1800.0 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]
+
+
+def test_clock_summary_reports_every_slowdown_reason():
+    s = _summary([_line(1200, 1965, hw="Active", hw_th="Active", sw_th="Active")])
+    assert s["reasons"] == ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"]
+
+
+def test_clock_summary_without_samples():
+    s = _summary([])
+    assert s["sm_mhz"] is None and s["samples"] == 0 and s["reasons"] == []
+
+
+def test_both_arms_name_the_same_workload_and_context():
+    for cfg, ctx in (("mistral-7b", 4096), ("llama-70b", 8192), ("tiny", 1024)):
+        bench.PROMPT_LEN, bench.DECODE_LEN = bench.WORKLOADS[cfg]
+        name = bench.workload_name(cfg)
+        assert name.startswith(cfg) and f"{bench.PROMPT_LEN}-token prompt" in name
+        assert bench.context_of(cfg) == ctx
+    bench.PROMPT_LEN, bench.DECODE_LEN = bench.WORKLOADS["mistral-7b"]
+    assert bench.workload_name("mistral-7b") == "mistral-7b batch-1 decode: 16-token prompt, decode positions 16..135"
