@@ -177,3 +177,15 @@ def test_noalloc_attention_size_limit_checked_on_the_host():
     assert str(L.yb_attention_scratch_bytes(32, 8, 128, 65536)) in msg  # the size the shape needs
     src = open(_lib.HEADER).read()
     assert "#define YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)" in src
+
+
+def test_no_cpu_fallback_without_a_gpu(tiny_yalm):
+    """Without a GPU the engine refuses to start (YB_E_CUDA from yb_create) instead of computing
+    anywhere else: the product path has no CPU fallback."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; this checks the behaviour without one")
+    m = Model(YALMData(tiny_yalm))
+    with pytest.raises(_lib.YalmB200Error) as ei:
+        m.cuda(0)
+    assert ei.value.code == _lib.YB_E_CUDA
