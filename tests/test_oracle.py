@@ -118,7 +118,7 @@ def test_restatement_vs_reference_gqa4_ring(tmp_path):
 
 
 def test_restatement_vs_reference_gelu(tmp_path):
-    """The GELU activation (yalm's default act_type, src/model.cpp:41-48; tanh form in its FFN)
+    """The GELU activation (yalm's default act_type, src/model.cpp:41-48; tanh form, src/infer.cpp:189-191)
     on a 2-layer tiny checkpoint: whole steps of the C restatement against yalm's CPU path."""
     from yalm_b200 import synth
     path = synth.write_yalm(str(tmp_path / "gelu.yalm"), synth.shape_with("tiny", n_layers=2, act_type="gelu"),
@@ -160,3 +160,24 @@ def test_restatement_vs_golden(tiny_yalm, golden):
     gaps = golden["top2_gap"][len(prompt) - 1:len(prompt) - 1 + len(greedy)]
     mism = [i for i, (a, b) in enumerate(zip(got_greedy, greedy)) if a != b]
     assert all(gaps[i] < 2e-3 for i in mism), (mism, gaps[mism] if mism else None)
+
+
+def test_golden_fixture_regenerates_from_the_reference(tiny_yalm, golden):
+    """tests/golden/make_golden.py run again on yalm's CPU path (oracle/_ref) reproduces the
+    committed fixture: same prompt, greedy ids, weight CRCs and KV bits, and logits to float
+    rounding."""
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location(
+        "make_golden", os.path.join(os.path.dirname(__file__), "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    fresh = mg.generate(tiny_yalm)
+    for key in ("prompt", "greedy", "logit_steps", "kv_layers", "kv_heads", "weight_crc"):
+        assert np.array_equal(fresh[key], golden[key]), key
+    assert list(fresh["weight_crc_names"]) == [str(n) for n in golden["weight_crc_names"]]
+    assert np.abs(fresh["logits"] - golden["logits"]).max() < 1e-5
+    assert np.abs(fresh["top2_gap"] - golden["top2_gap"]).max() < 1e-5
+    k_diff = np.count_nonzero(fresh["kv_k"] != golden["kv_k"])
+    v_diff = np.count_nonzero(fresh["kv_v"] != golden["kv_v"])
+    assert k_diff == 0 and v_diff == 0, (k_diff, v_diff)
