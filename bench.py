@@ -79,6 +79,15 @@ def workload_name(config: str) -> str:
             f"{PROMPT_LEN}..{PROMPT_LEN + DECODE_LEN - 1}")
 
 
+def yalm_generation_stats(prompt_len: int, decode_len: int, hydrate_s: float, s_per_token: float) -> dict:
+    """yalm's throughput definition (src/main.cpp:195-206): every token of the sequence (prompt and
+    generated) over the time of the prompt's hydrate plus the decode loop."""
+    total = hydrate_s + decode_len * s_per_token
+    n = prompt_len + decode_len
+    return {"tokens": n, "hydrate_s": round(hydrate_s, 4), "total_s": round(total, 4),
+            "throughput_tok_s": round(n / total, 1) if total > 0 else None}
+
+
 def context_of(config: str) -> int:
     """The context each config's checkpoint is opened with: yalm caps max_seq_len at 4096 unless a
     context is given (src/model.cpp:30-34); the 70B config asks for 8192."""
@@ -447,6 +456,10 @@ def main():
             "executor": executor,
             "prompt": {"tokens": PROMPT_LEN, "seconds": round(t_prompt, 4),
                        "tok_s": round(PROMPT_LEN / max(t_prompt, 1e-9), 1), "api": "yb_prefill"},
+            # yalm's own "Generation stats" (src/main.cpp:195-206): prompt plus generated tokens over the
+            # hydrate plus the decode loop, for this workload's prompt and DECODE_LEN generated tokens,
+            # the loop's per-token time taken from the yb_forward_sample loop above
+            "yalm_generation_stats": yalm_generation_stats(PROMPT_LEN, DECODE_LEN, t_prompt, t_e2e / max(e2e_steps, 1)),
             "engine_load": {"seconds": round(t_load, 2), "weight_bytes_per_rank": c.weight_bytes_per_token(world),
                             "gb_s": round(c.weight_bytes_per_token(world) / max(t_load, 1e-9) / 1e9, 1),
                             "source": "checkpoint pages in the host page cache (tmpfs)"},

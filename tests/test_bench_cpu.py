@@ -40,3 +40,9 @@ def test_both_arms_name_the_same_workload_and_context():
         assert bench.context_of(cfg) == ctx
     bench.PROMPT_LEN, bench.DECODE_LEN = bench.WORKLOADS["mistral-7b"]
     assert bench.workload_name("mistral-7b") == "mistral-7b batch-1 decode: 16-token prompt, decode positions 16..135"
+
+
+def test_yalm_generation_stats_definition():
+    """yalm's throughput (src/main.cpp:195-206): all tokens of the sequence over hydrate + decode."""
+    s = bench.yalm_generation_stats(16, 120, 0.5, 0.01)
+    assert s == {"tokens": 136, "hydrate_s": 0.5, "total_s": 1.7, "throughput_tok_s": 80.0}
