@@ -67,10 +67,12 @@ def test_warm_up_count_follows_the_command_line(fake_cuda):
     try:
         kbench._WARM = 0
         kbench._time(launch, 1)
-        assert calls == [0, 0]  # no warm-up: one launch per pass
+        assert calls == [0]  # no warm-up, and one timed pass below 3 launches (no percentiles)
+        assert kbench._LAST_SPREAD == {}
         calls.clear()
         kbench._WARM = 3
-        kbench._time(launch, 1)
-        assert calls == [0, 1, 2, 0, 0]
+        kbench._time(launch, 3)
+        assert calls == [0, 1, 2, 0, 1, 2, 0, 1, 2]
+        assert set(kbench._LAST_SPREAD) == {"p10_us", "p50_us", "p90_us"}
     finally:
         kbench._WARM = saved

@@ -43,10 +43,10 @@ _LAST_SPREAD: dict = {}
 def _time(fn, iters, warm=None):
     """Mean milliseconds per launch over `iters` back-to-back launches, and (kept in _LAST_SPREAD for
     the caller's JSON line) the per-launch p10 / p50 / p90 in microseconds from a second pass with an
-    event recorded after every launch.  An event makes the stream drain the kernel before the next
-    one starts, so the spread pass reads 1-3 us per launch above the mean pass for the short kernels;
-    the mean is the throughput figure.  Both passes queue their launches behind a device-side spin
-    (~30 us of SM cycles per launch), so host launch overhead enters neither."""
+    event recorded after every launch, when iters >= 3.  An event makes the stream drain the kernel
+    before the next one starts, so the spread pass reads 1-3 us per launch above the mean pass for
+    the short kernels; the mean is the throughput figure.  Both passes queue their launches behind a
+    device-side spin (~30 us of SM cycles per launch), so host launch overhead enters neither."""
     import torch
     for i in range(_WARM if warm is None else warm):
         fn(i)
@@ -60,6 +60,9 @@ def _time(fn, iters, warm=None):
     b.record()
     b.synchronize()
     mean_ms = a.elapsed_time(b) / iters
+    _LAST_SPREAD.clear()
+    if iters < 3:  # too few launches for percentiles; one pass keeps a profiler's launch count simple
+        return mean_ms
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(iters + 1)]
     torch.cuda._sleep(spin)
     ev[0].record()
@@ -68,7 +71,6 @@ def _time(fn, iters, warm=None):
         ev[i + 1].record()
     ev[-1].synchronize()
     per = np.array([ev[i].elapsed_time(ev[i + 1]) for i in range(iters)]) * 1000.0
-    _LAST_SPREAD.clear()
     _LAST_SPREAD.update({f"p{q}_us": round(float(np.percentile(per, q)), 2) for q in (10, 50, 90)})
     return mean_ms
 
