@@ -156,17 +156,23 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_baseline(path: str, context: int, n_decode: int, prompt_len: int = 2):
+def bench_prompt(vocab_size: int):
+    """The workload's prompt: PROMPT_LEN seeded random ids (both arms, and the GPU parity tests of
+    the benchmark configs, use these ids)."""
+    rng = np.random.default_rng(1234)
+    return [int(t) for t in rng.integers(0, vocab_size, PROMPT_LEN)]
+
+
+def cpu_baseline(path: str, context: int, n_decode: int, prompt):
     """yalm's own CPU decode path (oracle/_ref/ref_decode, built from the reference sources) on a
-    bounded sample of the same workload, all host cores."""
+    bounded sample of the same workload — the same prompt, then n_decode greedy steps at positions
+    len(prompt).. — with all host cores.  Returns its JSON record (per-step seconds, greedy ids)."""
     import oracle
     if not os.path.exists(oracle.REF_BIN):
         return None
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(99)
-    prompt = [str(int(t)) for t in rng.integers(0, 32000, prompt_len)]
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     env = dict(os.environ, OMP_NUM_THREADS=str(threads))
-    r = subprocess.run([oracle.REF_BIN, path, str(context), str(n_decode), str(threads)] + prompt,
+    r = subprocess.run([oracle.REF_BIN, path, str(context), str(n_decode), str(threads)] + [str(t) for t in prompt],
                        capture_output=True, text=True, env=env, timeout=1800)
     line = [l for l in r.stdout.splitlines() if l.startswith("{")]
     if r.returncode != 0 or not line:
@@ -189,18 +195,23 @@ def run_reference(args):
         return 0
     path = model_file(args.config, 0, 1, None)
     context = 8192 if args.config == "llama-70b" else 0
-    # Each step is one full decode token of the reference; the sample is bounded to keep the run
-    # to a few minutes (the 7B CPU path takes ~0.1-0.5 s per token).
-    n = max(1, min(args.steps, args.ref_max_steps))
-    d = cpu_baseline(path, context, n + args.warmup, prompt_len=2)
+    # The same prompt and positions as the GPU arm: W warm-up decode steps at PROMPT_LEN.., then the
+    # timed steps.  Each step is one full decode token of the reference; the sample stays inside the
+    # workload's decode positions (no wrap) and, for the 70B config (~4.5 s per CPU token), is
+    # bounded to keep the run to a few minutes.
+    cap = args.ref_max_steps if args.ref_max_steps else (8 if args.config == "llama-70b" else DECODE_LEN - args.warmup)
+    n = max(1, min(args.steps, cap))
+    prompt = bench_prompt(synth.SHAPES[args.config].vocab_size)
+    d = cpu_baseline(path, context, n + args.warmup, prompt)
     if d is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/ref_decode missing or failed"}))
         return 0
     steps = d["step_s"][args.warmup:]
     t = sum(steps)
     v = len(steps) / t
-    sample = (f"{len(steps)} timed decode tokens (+{args.warmup} warm-up) of the full {args.config} model after a "
-              f"2-token prompt, yalm -d cpu code path (Model::forward) via oracle/_ref/ref_decode")
+    sample = (f"{len(steps)} timed decode tokens at positions {PROMPT_LEN + args.warmup}..{PROMPT_LEN + args.warmup + len(steps) - 1} "
+              f"(+{args.warmup} warm-up) of the full {args.config} model after the workload's {PROMPT_LEN}-token "
+              f"prompt, yalm -d cpu code path (Model::forward) via oracle/_ref/ref_decode")
     print(json.dumps({
         "impl": "reference", "metric": METRICS[args.config], "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
         "steps": len(steps), "warmup": args.warmup, "ms_per_step": round(1000 * t / len(steps), 3),
@@ -212,6 +223,7 @@ def run_reference(args):
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
                          "sample": sample},
+        "greedy_ids": d["tokens"],
         "gpu_launches": 0,
     }))
     return 0
@@ -224,8 +236,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--config", default="mistral-7b", choices=["tiny", "mistral-7b", "llama-70b"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ref-max-steps", type=int, default=12)
-    ap.add_argument("--cpu-baseline-steps", type=int, default=6)
+    ap.add_argument("--ref-max-steps", type=int, default=0,
+                    help="cap on the reference arm's timed steps (default: the workload's decode positions)")
+    ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-profile", action="store_true")
     ap.add_argument("--no-long-context", action="store_true", help="skip the config-3 (3202-token prefill) phase")
@@ -270,9 +283,8 @@ def main():
         m.tp_join(ag)
     log(f"[bench] rank {rank}: engine ready in {time.time() - t:.1f}s")
     c = m.config
-    rng = np.random.default_rng(1234)
-    prompt = rng.integers(0, c.vocab_size, PROMPT_LEN)
-    stream_toks = rng.integers(0, c.vocab_size, 4096)
+    prompt = np.array(bench_prompt(c.vocab_size))
+    stream_toks = np.random.default_rng(1235).integers(0, c.vocab_size, 4096)
     s = InferenceState(c)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -317,15 +329,19 @@ def main():
     for pos, t_ in enumerate(prompt[:-1]):
         m.forward_async(int(t_), pos, InferenceMode.HYDRATE_KV_CACHE)
     tok = m.forward_sample(tok, PROMPT_LEN - 1)
+    greedy = [tok]  # free-running greedy ids from the prompt (positions PROMPT_LEN.. until the wrap)
     for i in range(args.warmup):
         tok = m.forward_sample(tok, pos_of(i))
+        greedy.append(tok)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
         tok = m.forward_sample(tok, pos_of(args.warmup + i))
+        greedy.append(tok)
     t_e2e = time.perf_counter() - t0
+    greedy = greedy[:DECODE_LEN]
     if world > 1:
         tt = torch.tensor([t_e2e], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -419,13 +435,20 @@ def main():
         long_ctx = long_context(m, c, args, stream, world, dist, peak)
 
     cpu = None
+    greedy_match = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config != "llama-70b" and args.dtype == "fp16":
-        d = cpu_baseline(path, context, args.cpu_baseline_steps)
+        d = cpu_baseline(path, context, args.cpu_baseline_steps, [int(t) for t in prompt])
         if d:
             st = d["step_s"]
             cpu = {"value": round(len(st) / sum(st), 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
-                   "sample": f"{len(st)} decode tokens of the full {args.config} model after a 2-token prompt, yalm "
-                             f"-d cpu code path (oracle/_ref/ref_decode), {d['threads']} OpenMP threads"}
+                   "sample": f"{len(st)} greedy decode tokens of the full {args.config} model after the workload's "
+                             f"{PROMPT_LEN}-token prompt, yalm -d cpu code path (oracle/_ref/ref_decode), "
+                             f"{d['threads']} OpenMP threads"}
+            ref_ids = [int(t) for t in d["tokens"]]
+            n = min(len(ref_ids), len(greedy))
+            greedy_match = {"steps": n, "match": greedy[:n] == ref_ids[:n], "engine": greedy[:n], "reference": ref_ids[:n],
+                            "how": "free-running greedy ids after the workload's prompt: yb_forward_sample (this arm's "
+                                   "e2e loop) vs yalm's CPU path (ref_decode, argmax, sampler.cpp:27-38)"}
 
     if world > 1:
         dist.barrier()
@@ -465,6 +488,7 @@ def main():
                             "source": "checkpoint pages in the host page cache (tmpfs)"},
             "graph_kernels_us": kernels,
             "cpu_baseline": cpu,
+            "greedy_match": greedy_match,
             "long_context": long_ctx,
             "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,

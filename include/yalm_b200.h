@@ -209,7 +209,9 @@ int yb_ffn(float* xout, const float* x, const uint16_t* w1, const uint16_t* w2, 
  * parity tests).  `stream` is a cudaStream_t (NULL = legacy default stream).  Asynchronous. */
 
 /* y (rows) = W (rows, cols) @ x, or y += W @ x when accumulate != 0.  norm_w (cols) non-NULL:
- * x is RMS-normalised first with eps (src/infer.cpp:136-146). */
+ * x is RMS-normalised first with eps (src/infer.cpp:136-146).  Rows wider than one kernel covers
+ * (fp16 beyond 14336 columns) run as equal column panels accumulated into y, as the engine runs
+ * w2 at hidden_dim 28672; norm_w must then be NULL. */
 int yb_gemv_dev(float* y, const float* x, const uint16_t* w, int rows, int cols, const float* norm_w, float eps,
                 int accumulate, void* stream);
 
@@ -248,7 +250,8 @@ size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int head_dim, int
  *    YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4 MiB: e.g. 32 heads of 128 at max_seq_len 30720); larger
  *    shapes return YB_E_INVALID with the sizes in yb_last_error().
  *  - The first call on each device looks up the array's device address (cudaGetSymbolAddress with
- *    that device current); make that first call before any stream capture on the device.
+ *    that device current), and the first call for each shape on a device sets up its launch (a
+ *    kernel attribute); make those first calls before any stream capture on the device.
  *  - All calls on a device share the one array, which keeps the previous call's contents (each
  *    call clears the part that must start at zero).  Calls whose executions overlap on the GPU, on
  *    different streams or host threads, race on it and give wrong results: order them on one

@@ -1,0 +1,207 @@
+"""End-to-end parity at the benchmark configurations (3 and 5), through the
+C ABI, against yalm's own CPU decode path (`Model::forward` on `-d cpu`, src/infer.cpp:483-528,
+driven like run_completion, src/main.cpp:160-190, by oracle/_ref):
+
+  * config 2 — the full 32-layer Mistral-7B checkpoint the bench decodes, with the bench's 16-token
+    prompt; the prompt goes in once through the per-token HYDRATE steps and once through the batched
+    yb_prefill; then 64 greedy steps.
+  * config 3 — the same architecture cut to 2 layers at context 4096, a 3202-token prompt (the
+    bench's long-context prompt), then decode steps at kv_len 3203.. .
+  * config 5 — the 70B-class architecture (dim 8192, 64 / 8 heads, SwiGLU 28672: the w2 matvec runs
+    as two column panels) cut to 2 layers at context 8192.
+
+Gates (the north star's): logits max-abs <= 2e-2 and cosine >= 0.9999 at every compared step,
+identical greedy ids.  Layer-truncated checkpoints keep every per-layer shape of the full model, so
+each matrix, attention and exchange shape the benchmark runs is covered; only the layer count
+differs (the CPU path cannot run 80 70B-sized layers in a test)."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from yalm_b200 import InferenceMode, InferenceState, Model, YALMData, synth
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_MAX_ABS = 2e-2
+LOGIT_COS = 0.9999
+
+
+def _cos(a, b):
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+def _checkpoint(base: str, **over) -> str:
+    shape = synth.shape_with(base, **over)
+    tag = "".join(f"_{k}{v}" for k, v in sorted(over.items()))
+    path = os.path.join(synth.scratch_dir(synth.file_bytes(shape)), f"yalm_{base}{tag}_seed0.yalm")
+    return synth.write_yalm(path, shape, seed=0)
+
+
+def _reference_run(ref, prompt, n_steps, logits_every=1):
+    """yalm's CPU path: the prompt in HYDRATE mode but the last token (main.cpp:171-177), then greedy
+    steps (sample_argmax, sampler.cpp:27-38).  Returns the greedy ids and the logits after the prompt
+    and after each step (every `logits_every`-th kept)."""
+    for pos, tok in enumerate(prompt[:-1]):
+        ref.forward(int(tok), pos, 0)
+    lg = ref.forward(int(prompt[-1]), len(prompt) - 1, 1)
+    ids, logits = [], {0: lg}
+    for i in range(n_steps):
+        tok = int(np.argmax(lg))
+        ids.append(tok)
+        lg = ref.forward(tok, len(prompt) + i, 1)
+        if (i + 1) % logits_every == 0 or i + 1 == n_steps:
+            logits[i + 1] = lg
+    return ids, logits
+
+
+def _check(got, exp, what):
+    d = float(np.abs(got - exp).max())
+    c = _cos(got, exp)
+    assert d <= LOGIT_MAX_ABS and c >= LOGIT_COS, f"{what}: max-abs {d:.3g}, cos {c:.7f}"
+    return d
+
+
+def _engine_teacher_forced(m, ref_ids, ref_logits, pos0, what):
+    """Feeds the reference's greedy ids; compares logits where the reference kept them and checks
+    that the engine's own argmax picks the reference's id at every step (the free-running greedy
+    sequences are then identical)."""
+    s = InferenceState(m.config)
+    worst = 0.0
+    lg = None
+    for i, tok in enumerate(ref_ids):
+        m.forward(s, int(tok), pos0 + i, InferenceMode.OUTPUT_LOGITS)
+        lg = s.logits()
+        if i + 1 in ref_logits:
+            worst = max(worst, _check(lg, ref_logits[i + 1], f"{what} step {i + 1}"))
+        if i + 1 < len(ref_ids):
+            assert int(np.argmax(lg)) == int(ref_ids[i + 1]), f"{what}: greedy id differs at step {i + 1}"
+    return worst
+
+
+# ---------------------------------------------------------------- config 2: Mistral-7B, 16-token prompt
+@pytest.fixture(scope="module")
+def mistral7b():
+    path = _checkpoint("mistral-7b")
+    rng = np.random.default_rng(1234)  # bench.py's prompt
+    prompt = [int(t) for t in rng.integers(0, 32000, 16)]
+    ref = oracle.RefModel(path)
+    ids, logits = _reference_run(ref, prompt, 64)
+    ref.close()
+    return path, prompt, ids, logits
+
+
+def test_mistral7b_per_token_prompt_then_64_greedy(gpu, mistral7b):
+    path, prompt, ids, logits = mistral7b
+    m = Model(YALMData(path)).cuda(0)
+    s = InferenceState(m.config)
+    for pos, tok in enumerate(prompt):
+        mode = InferenceMode.OUTPUT_LOGITS if pos + 1 == len(prompt) else InferenceMode.HYDRATE_KV_CACHE
+        m.forward(s, tok, pos, mode)
+    _check(s.logits(), logits[0], "after the prompt")
+    assert int(np.argmax(s.logits())) == ids[0]
+    worst = _engine_teacher_forced(m, ids, logits, len(prompt), "mistral-7b per-token prompt")
+    assert m.status() == 0
+    m.close()
+    print("mistral-7b per-token: worst logit max-abs", worst)
+
+
+def test_mistral7b_batched_prefill_then_64_greedy(gpu, mistral7b):
+    path, prompt, ids, logits = mistral7b
+    m = Model(YALMData(path)).cuda(0)
+    s = InferenceState(m.config)
+    m.prefill(prompt, 0, s)
+    _check(s.logits(), logits[0], "after yb_prefill")
+    assert int(np.argmax(s.logits())) == ids[0]
+    worst = _engine_teacher_forced(m, ids, logits, len(prompt), "mistral-7b batched prefill")
+    # free-running through the on-device sampler (bench.py's e2e call): the same 64 ids
+    m.prefill(prompt, 0)
+    tok = m.forward_sample(prompt[-1], len(prompt) - 1)
+    got = [tok]
+    for i in range(len(ids) - 1):
+        tok = m.forward_sample(tok, len(prompt) + i)
+        got.append(tok)
+    assert got == ids
+    assert m.status() == 0
+    m.close()
+    print("mistral-7b batched prefill: worst logit max-abs", worst)
+
+
+# ---------------------------------------------------------------- config 3: 3202-token prompt, context 4096
+@pytest.fixture(scope="module")
+def long_context_2layer():
+    path = _checkpoint("mistral-7b", n_layers=2)
+    rng = np.random.default_rng(4321)  # bench.py's long-context prompt
+    prompt = [int(t) for t in rng.integers(0, 32000, 3202)]
+    ref = oracle.RefModel(path, context=4096)
+    ids, logits = _reference_run(ref, prompt, 30, logits_every=3)
+    kv = {(l, g): ref.read_kv(l, g, 0, 3232) for l, g in ((0, 0), (1, 5))}
+    ref.close()
+    return path, prompt, ids, logits, kv
+
+
+@pytest.mark.parametrize("prompt_path", ["batched", "per_token"])
+def test_long_context_3202_prompt_then_decode(gpu, long_context_2layer, prompt_path):
+    path, prompt, ids, logits, kv = long_context_2layer
+    m = Model(YALMData(path), context=4096).cuda(0)
+    s = InferenceState(m.config)
+    if prompt_path == "batched":
+        m.prefill(prompt, 0, s)
+    else:
+        for pos, tok in enumerate(prompt[:-1]):
+            m.forward_async(tok, pos, InferenceMode.HYDRATE_KV_CACHE)
+        m.forward(s, prompt[-1], len(prompt) - 1, InferenceMode.OUTPUT_LOGITS)
+    _check(s.logits(), logits[0], f"after the 3202-token prompt ({prompt_path})")
+    assert int(np.argmax(s.logits())) == ids[0]
+    worst = _engine_teacher_forced(m, ids, logits, len(prompt), f"kv_len 3203..3232 ({prompt_path})")
+    m.sync()
+    # the cache the decode steps read, in fp16 ulps of the reference's value: layer 0's keys and
+    # values depend only on the embedding row and the weights (one ulp: yalm's -ffast-math rmsnorm
+    # sum runs in another order); layer 1's also carry layer 0's attention over up to 3232 slots;
+    # the batched path rounds its activations to fp16 for the tensor cores
+    ulps = {"per_token": (1.01, 4.0), "batched": (16.0, 16.0)}[prompt_path]
+    for (l, g), (kr, vr) in kv.items():
+        k, v = m.read_kv(l, g, 0, 3232)
+        for got, exp in ((k, kr), (v, vr)):
+            e = oracle.h2f(exp).astype(np.float64)
+            d = np.abs(oracle.h2f(got).astype(np.float64) - e)
+            ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(e), 2.0 ** -14))) - 10)
+            n_ulp = d / ulp
+            bad = float((n_ulp > ulps[min(l, 1)]).mean())
+            print(f"kv layer {l} head {g} ({prompt_path}): max {n_ulp.max():.2f} ulp, "
+                  f"{(d > 0).mean():.4f} differ, {bad:.2e} over the bound")
+            assert bad <= (0.0 if l == 0 and prompt_path == "per_token" else 1e-3), (l, g, prompt_path, bad)
+    assert m.status() == 0
+    m.close()
+    print(f"long context ({prompt_path}): worst logit max-abs", worst)
+
+
+# ---------------------------------------------------------------- config 5: 70B-class shape
+@pytest.fixture(scope="module")
+def llama70b_2layer():
+    path = _checkpoint("llama-70b", n_layers=2)
+    rng = np.random.default_rng(70)
+    prompt = [int(t) for t in rng.integers(0, 32000, 16)]
+    ref = oracle.RefModel(path, context=8192)
+    ids, logits = _reference_run(ref, prompt, 32)
+    ref.close()
+    return path, prompt, ids, logits
+
+
+@pytest.mark.parametrize("prompt_path", ["batched", "per_token"])
+def test_llama70b_shape_prompt_then_32_greedy(gpu, llama70b_2layer, prompt_path):
+    path, prompt, ids, logits = llama70b_2layer
+    m = Model(YALMData(path), context=8192).cuda(0)
+    s = InferenceState(m.config)
+    if prompt_path == "batched":
+        m.prefill(prompt, 0, s)
+    else:
+        for pos, tok in enumerate(prompt):
+            mode = InferenceMode.OUTPUT_LOGITS if pos + 1 == len(prompt) else InferenceMode.HYDRATE_KV_CACHE
+            m.forward(s, tok, pos, mode)
+    _check(s.logits(), logits[0], f"70B shape after the prompt ({prompt_path})")
+    worst = _engine_teacher_forced(m, ids, logits, len(prompt), f"70B shape ({prompt_path})")
+    assert m.status() == 0
+    m.close()
+    print(f"70B shape ({prompt_path}): worst logit max-abs", worst)

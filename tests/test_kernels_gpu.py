@@ -69,6 +69,24 @@ def test_gemv_matches_oracle(gpu, rows, cols):
     assert np.all(np.abs(y2.cpu().numpy() - (base + ref)) <= _tol(w, x) + 1e-6)
 
 
+@pytest.mark.parametrize("accumulate", [0, 1])
+def test_gemv_column_panels_70b_w2(gpu, accumulate):
+    """The 70B-class w2 (dim 8192 x hidden 28672): rows wider than one kernel covers run as two
+    14336-column panels with the full row stride, the second accumulating onto the first — the same
+    kernel instance and strides the engine launches for config 5's w2."""
+    import torch
+    rows, cols = 8192, 28672
+    rng = np.random.default_rng(70)
+    w = (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02).astype(np.float16).view(np.uint16)
+    x = rng.standard_normal(cols).astype(np.float32)
+    base = rng.standard_normal(rows).astype(np.float32)
+    y = _t(base) if accumulate else torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    _lib.call("yb_gemv_dev", _ptr(y), _ptr(_t(x)), _ptr(_t(w)), rows, cols, None, 0.0, accumulate, None)
+    _sync()
+    ref = oracle.matmul_f16(x, w) + (base if accumulate else 0)
+    assert np.all(np.abs(y.cpu().numpy() - ref) <= _tol(w, x) + 1e-6), np.abs(y.cpu().numpy() - ref).max()
+
+
 @pytest.mark.parametrize("rows,cols", [(4096, 4096), (32000, 4096), (4096, 512), (6, 8192)])
 def test_gemv_rmsnorm_prologue(gpu, rows, cols):
     import torch
@@ -205,13 +223,16 @@ def test_kv_append_indexing_integer_coded(gpu, pos, msl):
 @pytest.mark.parametrize("nh,nkv,hd,msl,kv_len", [
     (8, 2, 64, 1024, 1), (8, 2, 64, 1024, 2), (8, 2, 64, 1024, 31), (8, 2, 64, 1024, 33), (8, 2, 64, 1024, 96),
     (32, 8, 128, 4096, 1), (32, 8, 128, 4096, 65), (32, 8, 128, 4096, 129), (32, 8, 128, 4096, 3232),
-    (32, 8, 128, 4096, 4096), (64, 8, 128, 8192, 1152), (16, 16, 128, 512, 300), (16, 8, 64, 512, 511)])
+    (32, 8, 128, 4096, 4096), (64, 8, 128, 8192, 1152), (16, 16, 128, 512, 300), (16, 8, 64, 512, 511),
+    (32, 8, 128, 32768, 16384), (32, 8, 128, 32768, 32768)])
 def test_attention_matches_oracle(gpu, nh, nkv, hd, msl, kv_len):
+    """Includes config 4's long caches (kv_len 16384 and 32768 at max_seq_len 32768: the most
+    slices per kv head and the longest log-sum-exp merge)."""
     import torch
     rng = np.random.default_rng(kv_len + nh)
     q = rng.standard_normal(nh * hd).astype(np.float32)
-    k = rng.standard_normal((nkv, msl, hd)).astype(np.float16).view(np.uint16)
-    v = rng.standard_normal((nkv, msl, hd)).astype(np.float16).view(np.uint16)
+    k = rng.standard_normal((nkv, msl, hd), dtype=np.float32).astype(np.float16).view(np.uint16)
+    v = rng.standard_normal((nkv, msl, hd), dtype=np.float32).astype(np.float16).view(np.uint16)
     nbytes = _lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl)
     assert nbytes > 0
     scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")

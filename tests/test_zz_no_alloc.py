@@ -2,13 +2,15 @@
 time (a plugin inside a framework whose allocator owns the device memory, a serving loop that
 forbids allocation after start-up).  Checked through the C ABI against yb_attention_dev, which takes
 a caller-allocated scratch buffer, on two calls in a row (the library's fixed scratch array keeps the
-previous call's contents, so the second call checks it is reused correctly).  Kept in a file of its
-own that pytest collects last; it passes alone in a fresh process and after the other tests."""
+previous call's contents, so the second call checks it is reused correctly), and against the CPU
+oracle of yalm's attention.  Kept in a file of its own that pytest collects last; it passes alone in
+a fresh process and after the other tests."""
 import ctypes
 
 import numpy as np
 import pytest
 
+import oracle
 from yalm_b200 import _lib
 
 pytestmark = pytest.mark.gpu
@@ -20,30 +22,71 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-@pytest.mark.parametrize("nh,nkv,hd,msl,kv_len", [(32, 8, 128, 4096, 3232), (8, 2, 64, 1024, 65),
-                                                  (32, 8, 128, 4096, 1), (64, 8, 128, 8192, 1152)])
-def test_noalloc_attention_matches_allocating_entry_point(gpu, nh, nkv, hd, msl, kv_len):
+def _inputs(nh, nkv, hd, msl, seed):
     import torch
-    g = torch.Generator(device="cuda").manual_seed(kv_len + nh)
+    g = torch.Generator(device="cuda").manual_seed(seed)
     q = torch.randn(nh * hd, device="cuda", generator=g)
     k = torch.randn(nkv, msl, hd, device="cuda", generator=g).half()
     v = torch.randn(nkv, msl, hd, device="cuda", generator=g).half()
+    return q, k, v
+
+
+def _allocating(q, k, v, nh, nkv, hd, msl, kv_len):
+    import torch
     scratch = torch.zeros(_lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl), dtype=torch.uint8, device="cuda")
     ref = torch.zeros(nh * hd, device="cuda")
     _lib.call("yb_attention_dev", _p(ref), _p(q), _p(k), _p(v), nh, nkv, hd, msl, kv_len, _p(scratch), None)
     torch.cuda.synchronize()
+    return ref.cpu().numpy()
+
+
+def _noalloc(q, k, v, nh, nkv, hd, msl, kv_len):
+    import torch
+    out = torch.full((nh * hd,), float("nan"), device="cuda")
+    _lib.call("yb_attention_dev_noalloc", _p(out), _p(q), _p(k), _p(v), nh, nkv, hd, msl, kv_len, None)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def _oracle(q, k, v, nh, nkv, hd, msl, kv_len):
+    """yalm's attention (src/infer.cpp:394-415) restated in oracle/yalm_oracle.c."""
+    kc = k.cpu().numpy().view(np.uint16)[:, :kv_len]
+    vc = v.cpu().numpy().view(np.uint16)[:, :kv_len]
+    kb, vb = oracle.to_ref_kv_layout(kc, vc, msl)
+    return oracle.mha(q.cpu().numpy(), kb, vb, hd, kv_len, msl, nh, nkv)
+
+
+@pytest.mark.parametrize("nh,nkv,hd,msl,kv_len", [(32, 8, 128, 4096, 3232), (8, 2, 64, 1024, 65),
+                                                  (32, 8, 128, 4096, 1), (64, 8, 128, 8192, 1152)])
+def test_noalloc_attention_matches_allocating_entry_point(gpu, nh, nkv, hd, msl, kv_len):
+    q, k, v = _inputs(nh, nkv, hd, msl, kv_len + nh)
+    exp = _allocating(q, k, v, nh, nkv, hd, msl, kv_len)
+    cpu = _oracle(q, k, v, nh, nkv, hd, msl, kv_len)
     for call in range(2):
-        out = torch.full((nh * hd,), float("nan"), device="cuda")
-        _lib.call("yb_attention_dev_noalloc", _p(out), _p(q), _p(k), _p(v), nh, nkv, hd, msl, kv_len, None)
-        torch.cuda.synchronize()
-        got, exp = out.cpu().numpy(), ref.cpu().numpy()
+        got = _noalloc(q, k, v, nh, nkv, hd, msl, kv_len)
         assert np.isfinite(got).all(), call
         assert np.allclose(got, exp, rtol=RTOL, atol=ATOL), (call, np.abs(got - exp).max())
+        assert np.allclose(got, cpu, rtol=RTOL, atol=ATOL), (call, np.abs(got - cpu).max())
+
+
+def test_noalloc_attention_shape_changes_reuse_the_array(gpu):
+    """Shape A, then B, then A again: B's partial records take more of the array than A's, so the
+    place of A's merge counters lies inside B's partials and holds B's data when A runs again.  Each
+    call must clear what it needs and give the allocating entry point's result."""
+    shapes = [(32, 8, 128, 1024, 900), (32, 8, 128, 4096, 3232), (32, 8, 128, 1024, 900)]
+    sizes = [_lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl) for nh, nkv, hd, msl, _ in shapes]
+    assert sizes[1] > sizes[0]
+    for i, (nh, nkv, hd, msl, kv_len) in enumerate(shapes):
+        q, k, v = _inputs(nh, nkv, hd, msl, 100 + i)
+        exp = _allocating(q, k, v, nh, nkv, hd, msl, kv_len)
+        got = _noalloc(q, k, v, nh, nkv, hd, msl, kv_len)
+        assert np.allclose(got, exp, rtol=RTOL, atol=ATOL), (i, np.abs(got - exp).max())
 
 
 def test_noalloc_attention_rejects_oversized_shapes(gpu):
     import torch
-    nh, nkv, hd, msl = 64, 8, 128, 32768  # needs 64 * 256 * 130 * 4 bytes of scratch > 4 MiB
+    # needs 64 heads * 256 slices * (128 + 4) floats * 4 bytes of partials > 4 MiB
+    nh, nkv, hd, msl = 64, 8, 128, 32768
     assert _lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl) > (4 << 20)
     q = torch.zeros(nh * hd, device="cuda")
     kv = torch.zeros(1, dtype=torch.float16, device="cuda")

@@ -1,7 +1,6 @@
 """In-tree build of the native libraries.
 
   yalm_b200/libyalm_b200.so  — the decode engine (CUDA, sm_100a only) behind include/yalm_b200.h
-  yalm_b200/libyalm_synth.so — the host-side synthetic checkpoint filler used by synth.py
 
 Run `python -m yalm_b200.build` (or `__graft_entry__.build()`).  nvcc cross-compiles for sm_100a
 without a GPU.  Objects go to yalm_b200/_build/; rebuilds are incremental on source timestamps.
@@ -18,7 +17,6 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libyalm_b200.so")
-SYNTH_LIB = os.path.join(HERE, "libyalm_synth.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -67,19 +65,10 @@ def build_engine(verbose: bool = False, ptxas_info: bool = False) -> str:
     return LIB
 
 
-def build_synth() -> str:
-    src = os.path.join(CSRC, "synth_fill.c")
-    if _newer(SYNTH_LIB, [src]):
-        _run(["gcc", "-O3", "-fopenmp", "-fPIC", "-shared", "-std=c11", "-o", SYNTH_LIB, src, "-lm"])
-    return SYNTH_LIB
-
-
 def build_all(verbose: bool = False) -> None:
-    build_synth()
     build_engine(verbose=verbose)
 
 
 if __name__ == "__main__":
-    build_synth()
     build_engine(verbose=True, ptxas_info="--ptxas" in sys.argv)
     print(LIB)

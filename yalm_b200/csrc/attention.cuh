@@ -67,4 +67,9 @@ AttnPlan attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
 cudaError_t attn_prepare(const AttnPlan& p);  // once per plan, outside stream capture
 cudaError_t attn_launch(const AttnPlan& p, AttnArgs a, cudaStream_t stream, bool pdl);
 
+// The plan of a standalone launch, built and prepared (attn_prepare) on the first call for each
+// (device, shape) and looked up afterwards, so only that first call does host work and it must come
+// before any stream capture.  Returns 0 or a YB_E* code (message via yb_last_error).  capi.cu.
+int cached_attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len, AttnPlan* out);
+
 }  // namespace yb

@@ -71,6 +71,11 @@ int launch_gemv_common(GemvArgs a, int epi, cudaStream_t s) {
   return 0;
 }
 
+}  // namespace
+
+// Attention plans for standalone launches (yb_attention_dev, yb_attention_dev_noalloc), cached per
+// (device, shape): attn_prepare runs on the first call for a shape only.
+namespace yb {
 int cached_attn_plan(int nh, int nkv, int hd, int msl, AttnPlan* out) {
   int dev = 0;
   YB_CK(cudaGetDevice(&dev));
@@ -86,24 +91,35 @@ int cached_attn_plan(int nh, int nkv, int hd, int msl, AttnPlan* out) {
   *out = it->second;
   return 0;
 }
-
-}  // namespace
+}  // namespace yb
 
 extern "C" int yb_num_sms(void) { return current_sms(); }
 
 extern "C" int yb_gemv_dev(float* y, const float* x, const uint16_t* w, int rows, int cols, const float* norm_w,
                            float eps, int accumulate, void* stream) {
   if (!y || !x || !w || rows <= 0 || cols <= 0 || cols % 8) return set_error(YB_E_INVALID, "bad gemv arguments");
-  GemvArgs a = plain_args();
-  a.w = reinterpret_cast<const __half*>(w);
-  a.ldw = cols;
-  a.rows = rows;
-  a.cols = cols;
-  a.x = x;
-  a.norm_w = norm_w;
-  a.eps = eps;
-  a.y = y;
-  return launch_gemv_common(a, accumulate ? kEpiResid : kEpiStore, static_cast<cudaStream_t>(stream));
+  // column panels for rows wider than one kernel covers (the engine's w2 at hidden_dim 28672)
+  int panels = 1;
+  while (gemv_kpt_for(cols / panels, 2) < 0 || (cols / panels) % 8 || cols % panels)
+    if (++panels > 16) return set_error(YB_E_UNSUPPORTED, "no matvec configuration for cols=" + std::to_string(cols));
+  if (panels > 1 && norm_w)
+    return set_error(YB_E_UNSUPPORTED, "the RMSNorm prologue needs the whole row in one kernel (cols=" +
+                                           std::to_string(cols) + ")");
+  const int pcols = cols / panels;
+  for (int p = 0; p < panels; ++p) {
+    GemvArgs a = plain_args();
+    a.w = reinterpret_cast<const __half*>(w) + (size_t)p * pcols;
+    a.ldw = cols;
+    a.rows = rows;
+    a.cols = pcols;
+    a.x = x + (size_t)p * pcols;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.y = y;
+    int rc = launch_gemv_common(a, (accumulate || p > 0) ? kEpiResid : kEpiStore, static_cast<cudaStream_t>(stream));
+    if (rc) return rc;
+  }
+  return 0;
 }
 
 extern "C" int yb_gateup_dev(float* hb, const float* x, const uint16_t* w13, int hidden, int dim, const float* norm_w,

@@ -51,17 +51,21 @@ extern "C" int yb_attention_dev_noalloc(float* out, const float* q, const uint16
   using namespace yb;
   if (!out || !q || !k_cache || !v_cache || kv_len <= 0 || kv_len > max_seq_len)
     return set_error(YB_E_INVALID, "bad attention arguments");
-  AttnPlan p = attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len);
-  if (!p.ok) return set_error(YB_E_UNSUPPORTED, "no attention configuration for this shape");
-  const size_t part_bytes = (p.part_floats * 4 + 255) / 256 * 256;
+  // the size check needs only the shape (host arithmetic, no CUDA call)
+  const AttnPlan shape = attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len);
+  if (!shape.ok) return set_error(YB_E_UNSUPPORTED, "no attention configuration for this shape");
+  const size_t part_bytes = (shape.part_floats * 4 + 255) / 256 * 256;
   const size_t need = part_bytes + (size_t)n_kv_heads * 4;
   if (need > kNoAllocScratchBytes)
     return set_error(YB_E_INVALID, "attention scratch of " + std::to_string(need) + " bytes exceeds the " +
                                        std::to_string(kNoAllocScratchBytes) +
                                        "-byte fixed buffer of yb_attention_dev_noalloc (n_heads * "
                                        "ceil(max_seq_len / 128) * (head_dim + 4) * 4 + n_kv_heads * 4)");
+  AttnPlan p;
+  int rc = cached_attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len, &p);
+  if (rc) return rc;
   void* base = nullptr;
-  int rc = scratch_address(&base);
+  rc = scratch_address(&base);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned* counters = reinterpret_cast<unsigned*>(static_cast<char*>(base) + part_bytes);
@@ -78,7 +82,6 @@ extern "C" int yb_attention_dev_noalloc(float* out, const float* q, const uint16
   a.step = nullptr;
   a.kv_len = kv_len;
   a.max_seq_len = max_seq_len;
-  YB_CK(attn_prepare(p));
   YB_CK(attn_launch(p, a, s, false));
   return 0;
 }

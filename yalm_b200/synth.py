@@ -10,16 +10,12 @@ produces the same bytes.
 """
 from __future__ import annotations
 
-import ctypes
 import json
 import os
 import zlib
 from dataclasses import dataclass, asdict
 
 import numpy as np
-
-_HERE = os.path.dirname(os.path.abspath(__file__))
-
 
 @dataclass(frozen=True)
 class ModelShape:
@@ -118,25 +114,83 @@ def vocab_bytes(vocab_size: int) -> bytes:
 
 
 _DTYPE_SIZE = {"F16": 2, "F32": 4, "U8": 1, "F8_E5M2": 1}
-_lib = None
+
+# ---------------------------------------------------------------- seeded normal deviates
+# Element i of a tensor drawn with (seed, stream) is a deterministic function of those three numbers
+# only, so the contents do not depend on the thread count or on the order in which tensors are
+# written.  Each element pair takes one splitmix64 output; its two 32-bit halves are the uniforms of
+# a Box-Muller transform (float64), each deviate is rounded to float32, scaled by std in float32 and
+# rounded to fp16 (round to nearest even).  Pure numpy: the ufuncs release the GIL, so a thread per
+# core fills a 7B checkpoint at host memory speed.
+_U64 = np.uint64
 
 
-def _synth_lib():
-    global _lib
-    if _lib is None:
-        path = os.path.join(_HERE, "libyalm_synth.so")
-        if not os.path.exists(path):
-            from . import build as _build
-            _build.build_synth()
-        _lib = ctypes.CDLL(path)
-        _lib.synth_fill_normal_f16.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint64,
-                                               ctypes.c_uint64, ctypes.c_float]
-        _lib.synth_fill_const_f32.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_float]
-        _lib.synth_set_threads.argtypes = [ctypes.c_int]
-        _lib.synth_fill_normal_e5m2.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_uint64,
-                                                ctypes.c_uint64, ctypes.c_float]
-        _lib.synth_set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
-    return _lib
+def _splitmix64(z):
+    z = z + _U64(0x9E3779B97F4A7C15)
+    z ^= z >> _U64(30)
+    z *= _U64(0xBF58476D1CE4E5B9)
+    z ^= z >> _U64(27)
+    z *= _U64(0x94D049BB133111EB)
+    z ^= z >> _U64(31)
+    return z
+
+
+def _stream_key(seed: int, stream: int):
+    with np.errstate(over="ignore"):
+        return _splitmix64(_U64(seed) * _U64(0x2545F4914F6CDD1D) ^ _splitmix64(_U64(stream) + _U64(0x632BE59BD9B4E019)))
+
+
+def _normal_f16_pairs(key, p0: int, p1: int, std: float) -> np.ndarray:
+    """fp16 bit patterns of elements 2*p0 .. 2*p1 - 1."""
+    with np.errstate(over="ignore"):
+        r = np.arange(p0, p1, dtype=np.uint64)
+        r += key
+        r = _splitmix64(r)
+    u1 = (r >> _U64(32)).astype(np.float64)  # (0, 1]
+    u1 += 1.0
+    u1 *= 1.0 / 4294967296.0
+    ang = (r & _U64(0xFFFFFFFF)).astype(np.float64)  # 2 pi [0, 1)
+    ang *= 6.283185307179586 * (1.0 / 4294967296.0)
+    del r
+    np.log(u1, out=u1)
+    u1 *= -2.0
+    np.sqrt(u1, out=u1)
+    z = np.empty((p1 - p0, 2), np.float32)
+    np.multiply(u1, np.cos(ang), out=z[:, 0], casting="unsafe")
+    np.multiply(u1, np.sin(ang), out=z[:, 1], casting="unsafe")
+    z *= np.float32(std)
+    return z.reshape(-1).astype(np.float16).view(np.uint16)
+
+
+_CHUNK_PAIRS = 1 << 20
+
+
+def _threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def fill_normal(out: np.ndarray, seed: int, stream: int, std: float, e5m2: bool = False) -> None:
+    """Fills `out` (uint16 fp16 bits, or uint8 E5M2 bytes when e5m2) with std * N(0, 1) deviates of
+    (seed, stream).  An E5M2 value is the fp16 value of the same element rounded to nearest even on
+    its top byte (e5m2_from_f16_bits)."""
+    from concurrent.futures import ThreadPoolExecutor
+    n = out.size
+    pairs = (n + 1) // 2
+    key = _stream_key(seed, stream)
+
+    def work(p0):
+        p1 = min(p0 + _CHUNK_PAIRS, pairs)
+        e = min(2 * p1, n)
+        h = _normal_f16_pairs(key, p0, p1, std)[: e - 2 * p0]
+        out[2 * p0:e] = e5m2_from_f16_bits(h) if e5m2 else h
+
+    starts = range(0, pairs, _CHUNK_PAIRS)
+    if len(starts) <= 1:
+        for p0 in starts:
+            work(p0)
+        return
+    with ThreadPoolExecutor(min(_threads(), len(starts))) as ex:
+        list(ex.map(work, starts))
 
 
 def write_yalm(path: str, shape: ModelShape, seed: int = 0, std: float = 0.02) -> str:
@@ -163,23 +217,21 @@ def write_yalm(path: str, shape: ModelShape, seed: int = 0, std: float = 0.02) -
             n = int.from_bytes(f.read(8), "little")
             if f.read(n) == hjson:
                 return path
-    lib = _synth_lib()
     tmp = path + ".tmp"
     with open(tmp, "wb") as f:
         f.write(len(hjson).to_bytes(8, "little"))
         f.write(hjson)
         f.truncate(total)
     mm = np.memmap(tmp, dtype=np.uint8, mode="r+")
-    base = mm.ctypes.data + data_start
     for name, dt, shp in specs:
         o0, o1 = header[name]["data_offsets"]
-        n = int(np.prod(shp))
+        view = mm[data_start + o0: data_start + o1]
         if dt == "F32":
-            lib.synth_fill_const_f32(base + o0, n, 1.0)
+            view.view(np.float32)[:] = 1.0
         elif dt == "F8_E5M2":
-            lib.synth_fill_normal_e5m2(base + o0, n, seed, zlib.crc32(name.encode()), std)
+            fill_normal(view, seed, zlib.crc32(name.encode()), std, e5m2=True)
         else:
-            lib.synth_fill_normal_f16(base + o0, n, seed, zlib.crc32(name.encode()), std)
+            fill_normal(view.view(np.uint16), seed, zlib.crc32(name.encode()), std)
     o0, _ = header["tokenizer.tokens"]["data_offsets"]
     mm[data_start + o0: data_start + o0 + len(tok)] = np.frombuffer(tok, dtype=np.uint8)
     mm.flush()
