@@ -20,17 +20,43 @@ OUT = os.path.join(HERE, "_ref")
 REF_LIB = os.path.join(OUT, "libyalm_ref.so")
 C_LIB = os.path.join(OUT, "libyalm_oracle.so")
 REF_BIN = os.path.join(OUT, "ref_decode")
-REF_SRC = os.environ.get("YALM_REF_SRC", "/root/reference")
+REF_BIN_GPU = os.path.join(OUT, "ref_decode_gpu")
+REF_KERNELS = os.path.join(OUT, "ref_kernels")
+YALM_MAIN = os.path.join(OUT, "yalm_main")
+YALM_MAIN_B200 = os.path.join(OUT, "yalm_main_b200")
+
+
+def _reference_root():
+    """Where yalm's sources are: $YALM_REF_SRC, else the `reference_path` BASELINE.json names (the
+    build container); None where neither exists (the prebuilt oracle/_ref is then used as is)."""
+    p = os.environ.get("YALM_REF_SRC")
+    if not p:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                p = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            p = None
+    return p if p and os.path.isfile(os.path.join(p, "src", "model.h")) else None
+
+
+REF_SRC = _reference_root()
 
 _P, _I, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
 
 
-def build(force: bool = False) -> None:
-    """Builds the C restatement always, and the reference objects when the sources are present."""
+def build(force: bool = False, gpu: bool = False, b200: bool = False) -> None:
+    """Builds the C restatement always, and, when yalm's sources are present, yalm's CPU path; with
+    gpu also its CUDA backends (sm_100a) and CLI, with b200 its CLI patched for the -d b200 device
+    (needs libyalm_b200.so)."""
     targets = ["oracle"]
-    if os.path.isdir(os.path.join(REF_SRC, "src")):
+    if REF_SRC:
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_SRC}"] + targets, check=True)
+        if gpu:
+            targets.append("ref-gpu")
+        if b200:
+            targets.append("ref-b200")
+    subprocess.run(["make", "-s", "-C", HERE, f"REF={REF_SRC or ''}", f"-j{os.cpu_count() or 4}"] + targets, check=True)
 
 
 def _load(path):

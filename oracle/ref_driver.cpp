@@ -1,16 +1,13 @@
 // TEST INFRASTRUCTURE ONLY — never linked into, loaded by, or called from the product library.
 //
-// Drives yalm's own CPU decode path (`Model::forward` -> `_forward_cpu`, src/infer.cpp:483-528) so
-// that tests and the bench's reference arm can compare against, and time, the reference itself.
-// The reference sources are compiled where they lie (see oracle/Makefile); this file only adds:
-//   * a flat extern "C" surface for ctypes (open a .yalm file, step the model, read logits / KV);
-//   * definitions for the CUDA-side symbols that src/model.cpp references but that the CPU path
-//     never calls (upload_cuda & co from src/infer.cu:60-91, the coop entry points from
-//     src/coop.h:5-6, libgemm_init from src/libgemm.h:12, and the `_block_cuda*` /
-//     `_forward_cuda*` members).  Each aborts: reaching one means the CPU path was not taken.
+// Drives yalm's own decode path (`Model::forward`, src/model.cpp:479-494: `_forward_cpu`,
+// src/infer.cpp:483-528, or on a device the CUDA backends of src/infer.cu / src/coop.cu) so that
+// tests and the bench's reference arm can compare against, and time, the reference itself.  The
+// reference sources are compiled where they lie (see oracle/Makefile); this file only adds a flat
+// extern "C" surface for ctypes and the drivers (open a .yalm file, move it to a device, step the
+// model, read logits / KV).  Linked either with ref_cuda_stubs.cpp (the CPU-only build) or with the
+// reference's own CUDA objects (the GPU build).
 #include "model.h"
-#include "coop.h"
-#include "libgemm.h"
 
 #include <cstdio>
 #include <cstdlib>
@@ -18,32 +15,6 @@
 #include <memory>
 #include <omp.h>
 #include <string>
-
-[[noreturn]] static void not_cpu(const char* what) {
-  std::fprintf(stderr, "oracle/ref_driver: CUDA symbol %s reached on the CPU path\n", what);
-  std::abort();
-}
-
-// ---- CUDA-side symbols referenced from src/model.cpp, unused on the CPU path ----
-extern "C" void* upload_cuda(void*, size_t) { not_cpu("upload_cuda"); }
-extern "C" void* download_cuda(void*, size_t, std::string) { not_cpu("download_cuda"); }
-extern "C" void register_cuda_host(void*, size_t) { not_cpu("register_cuda_host"); }
-extern "C" void free_cuda(void*) { not_cpu("free_cuda"); }
-extern "C" void unregister_cuda_host(void*) { not_cpu("unregister_cuda_host"); }
-extern "C" void set_cuda_device(int) { not_cpu("set_cuda_device"); }
-extern "C" void init_cuda_stream(cudaStream_t*) { not_cpu("init_cuda_stream"); }
-void yalm_coop_prepare(Model&) { not_cpu("yalm_coop_prepare"); }
-void yalm_coop_forward(Model&, InferenceState&, int, int, InferenceMode) { not_cpu("yalm_coop_forward"); }
-void libgemm_init(cudaStream_t, LibGemmBackend) { not_cpu("libgemm_init"); }
-template <typename T>
-void Block::_block_cuda(InferenceState&, int, int, int, int) const { not_cpu("Block::_block_cuda"); }
-template <typename T>
-void Block::_block_cuda_lib(InferenceState&, int, int, int, int) const { not_cpu("Block::_block_cuda_lib"); }
-template void Block::_block_cuda<float>(InferenceState&, int, int, int, int) const;
-template void Block::_block_cuda<f16_t>(InferenceState&, int, int, int, int) const;
-template void Block::_block_cuda_lib<f16_t>(InferenceState&, int, int, int, int) const;
-void Model::_forward_cuda(InferenceState&, int, int, InferenceMode) { not_cpu("Model::_forward_cuda"); }
-void Model::_forward_cuda_lib(InferenceState&, int, int, InferenceMode) { not_cpu("Model::_forward_cuda_lib"); }
 
 // ---- flat surface for ctypes ----
 struct RefHandle {
@@ -109,6 +80,27 @@ void ref_read_kv(void* hp, int layer, int kvh, int pos0, int n, uint16_t* k_out,
 }
 
 void ref_close(void* hp) { delete static_cast<RefHandle*>(hp); }
+
+// Moves the model and state to a device the way run_completion's setup_cuda does
+// (src/main.cpp:57-86): "cuda" = Model::cuda() + InferenceState::cuda() (the CUDA-graph backend),
+// "cuda-coop" = the cooperative backend.  Returns 0, or -1 for an unknown device name.  In the
+// CPU-only build the CUDA symbols are stubs that abort.
+int ref_to_device(void* hp, const char* device) {
+  auto* h = static_cast<RefHandle*>(hp);
+  const std::string d = device;
+  if (d == "cpu") return 0;
+  if (d == "cuda") {
+    h->model->cuda();
+    h->state->cuda();
+    return 0;
+  }
+  if (d == "cuda-coop") {
+    h->model->cuda_coop();
+    h->state->cuda_coop();
+    return 0;
+  }
+  return -1;
+}
 
 // Kernel-level hooks: the reference's own CPU test entry points (src/model.h:340-367).
 void ref_matmul_f16(float* xout, float* x, uint16_t* w, int n, int d) { matmul_cpu(xout, x, w, n, d); }
