@@ -113,12 +113,13 @@ int yb_forward_prob(yb_engine* e, int token, int pos, int target, float* prob);
 
 /* Replaces the prompt loop of yalm's run_completion (src/main.cpp:171-177: every prompt token
  * through Model::forward, HYDRATE_KV_CACHE but the last): tokens[0..n) at positions pos0 .. pos0+n-1
- * go through the model in one batched pass (tensor-core GEMMs, causal attention over the cached and
- * new slots), filling the KV cache; with logits non-null the last token's logits are written there,
- * as yb_forward in OUTPUT_LOGITS mode would.  Activations of the batched pass are rounded to fp16 for
- * the tensor cores, so cache values may differ from the per-token path by fp16 rounding.  Engines
- * or prompts the batched pass does not cover (tensor parallel, fp8 weights, GELU, positions past the
- * context, one token) run the per-token steps.  Returns after completion. */
+ * go through the model, filling the KV cache: all but the last token in one batched pass (tensor-core
+ * GEMMs, causal attention over the cached and new slots), the last token as one decode step
+ * (yb_forward), whose logits are written to `logits` when it is non-null.  Activations of the
+ * batched pass are rounded to fp16 for the tensor cores, so the cache slots of the earlier prompt
+ * tokens may differ from the per-token path by that rounding.  Engines or prompts the batched pass
+ * does not cover (tensor parallel, fp8 weights, GELU, positions past the context, fewer than three
+ * tokens) run the per-token steps.  Returns after completion. */
 int yb_prefill(yb_engine* e, const int* tokens, int n, int pos0, float* logits);
 
 /* Same step, logits left on the device (yb_logits_dev) and no host synchronisation: for

@@ -1,5 +1,7 @@
 """Generates tests/golden/tiny_golden.npz from yalm's own CPU path (oracle/_ref, built from the
-reference sources) on the seeded synthetic tiny checkpoint (config 1 of the benchmark configs).
+reference sources) on the seeded synthetic tiny checkpoint (config 1 of the benchmark configs), and
+tests/golden/kv8_golden.npz (generate_kv8) on a small 8-kv-head checkpoint for the tensor-parallel
+check of bench.py.
 
 Contents:
   prompt          32 token ids, uniform in [0, 4096), numpy default_rng(1234)
@@ -63,12 +65,67 @@ def generate(path: str):
                 weight_crc_names=np.array(names), weight_crc=np.array([crc[n] for n in names], np.uint32))
 
 
+# The tensor-parallel check of bench.py --gpus N: a small checkpoint with 8 kv heads (so it splits 8
+# ways), forced token ids with the reference's logits at a few steps, and a greedy run.
+KV8_SHAPE = dict(dim=1024, n_heads=16, n_kv_heads=8, head_dim=64, hidden_dim=2816)
+KV8_SEED = 3
+KV8_FORCED, KV8_PROMPT, KV8_GREEDY = 24, 16, 16
+KV8_LOGIT_STEPS = [0, 5, 11, 17, 22, 23]
+
+
+def kv8_shape():
+    return synth.shape_with("tiny", **KV8_SHAPE)
+
+
+def generate_kv8(path: str):
+    """kv8_golden.npz:
+      forced          24 token ids (default_rng(8)), each step in OUTPUT_LOGITS mode from position 0
+      logit_steps     steps whose logits are stored;  logits  float32 [len(logit_steps), 4096]
+      prompt          16 token ids; greedy: 16 greedy ids after it;  greedy_gap: top-1 minus top-2
+                      logit before each greedy id
+      weight_crc      crc32 of the first 4096 bytes of every tensor (pins the synthetic generator)"""
+    ref = oracle.RefModel(path)
+    rng = np.random.default_rng(8)
+    forced = rng.integers(0, ref.vocab_size, KV8_FORCED).astype(np.int32)
+    prompt = rng.integers(0, ref.vocab_size, KV8_PROMPT).astype(np.int32)
+    keep = []
+    for pos, tok in enumerate(forced):
+        lg = ref.forward(int(tok), pos, 1)
+        if pos in KV8_LOGIT_STEPS:
+            keep.append(lg.copy())
+    ref.close()
+    ref = oracle.RefModel(path)
+    lg = None
+    for pos, tok in enumerate(prompt):
+        lg = ref.forward(int(tok), pos, 1 if pos + 1 == len(prompt) else 0)
+    greedy, gaps = [], []
+    for i in range(KV8_GREEDY):
+        srt = np.sort(lg)
+        gaps.append(srt[-1] - srt[-2])
+        tok = int(np.argmax(lg))
+        greedy.append(tok)
+        lg = ref.forward(tok, len(prompt) + i, 1)
+    y = YALMData(path)
+    crc = {n: zlib.crc32(bytes(y.buf[t.offset:t.offset + min(4096, t.size)])) for n, t in y.tensors.items()}
+    names = sorted(crc)
+    return dict(forced=forced, logit_steps=np.array(KV8_LOGIT_STEPS, np.int32), logits=np.stack(keep).astype(np.float32),
+                prompt=prompt, greedy=np.array(greedy, np.int32), greedy_gap=np.array(gaps, np.float32),
+                weight_crc_names=np.array(names), weight_crc=np.array([crc[n] for n in names], np.uint32))
+
+
 if __name__ == "__main__":
     import tempfile
+    here = os.path.dirname(os.path.abspath(__file__))
     path = os.path.join(tempfile.gettempdir(), "yalm_tiny_seed0.yalm")
     synth.write_yalm(path, synth.SHAPES["tiny"], seed=0)
     out = generate(path)
-    dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tiny_golden.npz")
+    dst = os.path.join(here, "tiny_golden.npz")
     np.savez_compressed(dst, **out)
     print("wrote", dst, os.path.getsize(dst), "bytes; greedy", out["greedy"][:16], "min top2 gap",
           float(out["top2_gap"].min()))
+    path = os.path.join(tempfile.gettempdir(), f"yalm_kv8_seed{KV8_SEED}.yalm")
+    synth.write_yalm(path, kv8_shape(), seed=KV8_SEED)
+    out = generate_kv8(path)
+    dst = os.path.join(here, "kv8_golden.npz")
+    np.savez_compressed(dst, **out)
+    print("wrote", dst, os.path.getsize(dst), "bytes; greedy", out["greedy"], "min gap", float(out["greedy_gap"].min()))

@@ -156,22 +156,24 @@ def test_long_context_3202_prompt_then_decode(gpu, long_context_2layer, prompt_p
     assert int(np.argmax(s.logits())) == ids[0]
     worst = _engine_teacher_forced(m, ids, logits, len(prompt), f"kv_len 3203..3232 ({prompt_path})")
     m.sync()
-    # the cache the decode steps read, in fp16 ulps of the reference's value: layer 0's keys and
-    # values depend only on the embedding row and the weights (one ulp: yalm's -ffast-math rmsnorm
-    # sum runs in another order); layer 1's also carry layer 0's attention over up to 3232 slots;
-    # the batched path rounds its activations to fp16 for the tensor cores
-    ulps = {"per_token": (1.01, 4.0), "batched": (16.0, 16.0)}[prompt_path]
+    # the cache the decode steps read: each value within one fp16 ulp of the reference's plus a
+    # share of its slot's RMS.  The per-token path differs from yalm's only in the order of sums
+    # (yalm's -ffast-math rmsnorm) and in the last bits of the RoPE angles, which a value that is a
+    # difference of two near-equal products magnifies; on the batched path every activation entering
+    # a GEMM is rounded to fp16 (2^-11 relative), which moves each output by about that share of its
+    # row's magnitude, and layer 1 inherits layer 0's attention error over up to 3232 slots.
+    alpha = {"per_token": 2.0 ** -10, "batched": 2.0 ** -7}[prompt_path]
     for (l, g), (kr, vr) in kv.items():
         k, v = m.read_kv(l, g, 0, 3232)
-        for got, exp in ((k, kr), (v, vr)):
+        for name, got, exp in (("k", k, kr), ("v", v, vr)):
             e = oracle.h2f(exp).astype(np.float64)
             d = np.abs(oracle.h2f(got).astype(np.float64) - e)
             ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(e), 2.0 ** -14))) - 10)
-            n_ulp = d / ulp
-            bad = float((n_ulp > ulps[min(l, 1)]).mean())
-            print(f"kv layer {l} head {g} ({prompt_path}): max {n_ulp.max():.2f} ulp, "
-                  f"{(d > 0).mean():.4f} differ, {bad:.2e} over the bound")
-            assert bad <= (0.0 if l == 0 and prompt_path == "per_token" else 1e-3), (l, g, prompt_path, bad)
+            rms = np.sqrt((e * e).mean(axis=1, keepdims=True))
+            rel = (d / rms).max()
+            print(f"{name} layer {l} head {g} ({prompt_path}): max |diff| / slot rms {rel:.2e}, "
+                  f"{(d > 0).mean():.4f} of values differ")
+            assert np.all(d <= ulp + alpha * rms), (name, l, g, prompt_path, rel)
     assert m.status() == 0
     m.close()
     print(f"long context ({prompt_path}): worst logit max-abs", worst)

@@ -224,10 +224,12 @@ def test_kv_append_indexing_integer_coded(gpu, pos, msl):
     (8, 2, 64, 1024, 1), (8, 2, 64, 1024, 2), (8, 2, 64, 1024, 31), (8, 2, 64, 1024, 33), (8, 2, 64, 1024, 96),
     (32, 8, 128, 4096, 1), (32, 8, 128, 4096, 65), (32, 8, 128, 4096, 129), (32, 8, 128, 4096, 3232),
     (32, 8, 128, 4096, 4096), (64, 8, 128, 8192, 1152), (16, 16, 128, 512, 300), (16, 8, 64, 512, 511),
-    (32, 8, 128, 32768, 16384), (32, 8, 128, 32768, 32768)])
+    (32, 8, 128, 32768, 16384), (32, 8, 128, 32768, 32768), (8, 2, 128, 8192, 8192), (4, 1, 128, 16384, 16000),
+    (8, 1, 64, 4096, 2049), (64, 8, 128, 8192, 8192)])
 def test_attention_matches_oracle(gpu, nh, nkv, hd, msl, kv_len):
-    """Includes config 4's long caches (kv_len 16384 and 32768 at max_seq_len 32768: the most
-    slices per kv head and the longest log-sum-exp merge)."""
+    """Includes config 4's long caches (kv_len 16384 and 32768 at max_seq_len 32768: 2048 slots per
+    CTA of a 16-CTA cluster) and long caches of one or two kv heads, which several clusters per kv
+    head share and merge through the scratch records."""
     import torch
     rng = np.random.default_rng(kv_len + nh)
     q = rng.standard_normal(nh * hd).astype(np.float32)

@@ -57,7 +57,8 @@ def _oracle(q, k, v, nh, nkv, hd, msl, kv_len):
 
 
 @pytest.mark.parametrize("nh,nkv,hd,msl,kv_len", [(32, 8, 128, 4096, 3232), (8, 2, 64, 1024, 65),
-                                                  (32, 8, 128, 4096, 1), (64, 8, 128, 8192, 1152)])
+                                                  (32, 8, 128, 4096, 1), (64, 8, 128, 8192, 1152),
+                                                  (8, 2, 128, 8192, 6000)])
 def test_noalloc_attention_matches_allocating_entry_point(gpu, nh, nkv, hd, msl, kv_len):
     q, k, v = _inputs(nh, nkv, hd, msl, kv_len + nh)
     exp = _allocating(q, k, v, nh, nkv, hd, msl, kv_len)
@@ -70,10 +71,11 @@ def test_noalloc_attention_matches_allocating_entry_point(gpu, nh, nkv, hd, msl,
 
 
 def test_noalloc_attention_shape_changes_reuse_the_array(gpu):
-    """Shape A, then B, then A again: B's partial records take more of the array than A's, so the
-    place of A's merge counters lies inside B's partials and holds B's data when A runs again.  Each
-    call must clear what it needs and give the allocating entry point's result."""
-    shapes = [(32, 8, 128, 1024, 900), (32, 8, 128, 4096, 3232), (32, 8, 128, 1024, 900)]
+    """Shape A, then B, then A again, both long caches of two kv heads, whose clusters merge through
+    the array: B's cluster records take more of it than A's, so the place of A's merge counters lies
+    inside B's records and holds B's data when A runs again.  Each call must clear what it needs and
+    give the allocating entry point's result."""
+    shapes = [(8, 2, 128, 4096, 3000), (16, 2, 128, 8192, 8000), (8, 2, 128, 4096, 3000)]
     sizes = [_lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl) for nh, nkv, hd, msl, _ in shapes]
     assert sizes[1] > sizes[0]
     for i, (nh, nkv, hd, msl, kv_len) in enumerate(shapes):
@@ -85,8 +87,8 @@ def test_noalloc_attention_shape_changes_reuse_the_array(gpu):
 
 def test_noalloc_attention_rejects_oversized_shapes(gpu):
     import torch
-    # needs 64 heads * 256 slices * (128 + 4) floats * 4 bytes of partials > 4 MiB
-    nh, nkv, hd, msl = 64, 8, 128, 32768
+    # needs 32 kv heads * 32 clusters * 8 heads * (128 + 2) floats * 4 bytes of records > 4 MiB
+    nh, nkv, hd, msl = 256, 32, 128, 4096
     assert _lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl) > (4 << 20)
     q = torch.zeros(nh * hd, device="cuda")
     kv = torch.zeros(1, dtype=torch.float16, device="cuda")

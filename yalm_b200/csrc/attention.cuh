@@ -1,6 +1,7 @@
-// Split-K GQA decode attention (see attention.cu).
+// GQA decode attention, one thread-block cluster per kv head (see attention.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 
@@ -8,23 +9,22 @@
 
 namespace yb {
 
-constexpr int kAttnCapacity = 128;  // cache slots one CTA covers (8 warps x 16)
-
 struct AttnArgs {
   const float* q;         // [n_heads][head_dim]
   const __half* k_cache;  // [n_kv_heads][max_seq_len][head_dim]
   const __half* v_cache;  // [n_kv_heads][max_seq_len][head_dim]
   float* out;             // [n_heads][head_dim]
-  float* part;            // [n_heads][s_max][head_dim + 4] slice partials (o, m, l, padding)
+  float* part;            // [n_kv_heads][clusters][GQ][head_dim + 2] cluster records (o, m, l) of the
+                          // merge over clusters (AttnPlan::part_floats; unused with one cluster)
   unsigned* counters;     // [n_kv_heads], zero between launches
   const StepState* step;  // kv_len is read from here when non-null ...
   int kv_len;             // ... else from here
   int max_seq_len;
+  int cta_slots;          // slots per CTA before a kv head's cache splits over more CTAs (0: 128)
   unsigned* status;
   // optional timeline (null = off): per CTA c = blockIdx.y * gridDim.x + blockIdx.x,
-  // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 1 inputs ready, 2 K/V rows staged,
-  // 5 slot groups done (thread 0), 3 slice partial written, 4 exit (inactive slices stamp only 0
-  // and 1)
+  // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 1 inputs ready, 2 first stage landed,
+  // 5 slots folded (thread 0), 3 CTA record written, 4 exit (CTAs of idle clusters stamp only 0)
   unsigned long long* trace;
   int trace_stride;
 };
@@ -32,40 +32,28 @@ struct AttnArgs {
 struct AttnPlan {
   bool ok;
   const void* fn;
-  dim3 grid;
-  int s_max;
+  dim3 grid;           // (cluster * clusters per kv head, n_kv_heads)
+  int cluster;         // CTAs per cluster
+  int s_max;           // bound on the clusters per kv head (sizes the scratch)
+  int max_seq_len;
   size_t smem;
-  size_t part_floats;
+  size_t part_floats;  // scratch floats for the merge over clusters, valid for any device
 };
 
-// Shared memory of one attention CTA: a region holding the staged K/V rows, or, when larger and
-// below kAttnMergeSmemMax, the slice partials of one kv head (merged in shared memory); then the
-// warp-combine buffer and the barriers.
-constexpr size_t kAttnMergeSmemMax = 96 * 1024;
-// Shared-memory row of a staged cache slot: head_dim fp16 padded by 16 bytes (an odd multiple of 16).
-__host__ __device__ constexpr int attn_row_bytes(int hd) { return hd * 2 + 16; }
-__host__ __device__ constexpr size_t attn_stage_bytes(int hd) { return (size_t)2 * kAttnCapacity * attn_row_bytes(hd); }
-__host__ __device__ constexpr size_t attn_merge_bytes(int hd, int gq, int s_max) {
-  return (size_t)gq * s_max * (hd + 4) * 4 + (size_t)2 * gq * s_max * 4;
-}
-__host__ __device__ constexpr bool attn_merge_in_smem(int hd, int gq, int s_max) {
-  return attn_merge_bytes(hd, gq, s_max) <= kAttnMergeSmemMax;
-}
-__host__ __device__ constexpr size_t attn_region_bytes(int hd, int gq, int s_max) {
-  return attn_merge_in_smem(hd, gq, s_max) && attn_merge_bytes(hd, gq, s_max) > attn_stage_bytes(hd)
-             ? (attn_merge_bytes(hd, gq, s_max) + 127) / 128 * 128
-             : attn_stage_bytes(hd);
-}
+// TMA tensor maps of one layer's K and V caches: [n_kv_heads * max_seq_len][head_dim] fp16 read in
+// 64-slot x 64-dim boxes with the 128-byte swizzle.
+struct AttnMaps {
+  CUtensorMap k, v;
+};
+bool attn_maps(AttnMaps* m, const __half* k_cache, const __half* v_cache, int n_kv_heads, int max_seq_len,
+               int head_dim);
 
-// Warp-combine buffer: per warp and head the output row (head_dim + 4 floats), max and sum, the
-// warp weights, then per head the CTA max and sum.
-__host__ __device__ constexpr size_t attn_red_bytes(int hd, int gq) {
-  return ((size_t)8 * gq * (hd + 4) + (size_t)8 * gq * 3 + (size_t)2 * gq) * 4;
-}
-
+// The shape's kernel, shared memory and a device-independent scratch bound (host arithmetic only).
 AttnPlan attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
-cudaError_t attn_prepare(const AttnPlan& p);  // once per plan, outside stream capture
-cudaError_t attn_launch(const AttnPlan& p, AttnArgs a, cudaStream_t stream, bool pdl);
+// Once per plan and device, outside stream capture: kernel attributes, and the cluster size and
+// clusters per kv head from the device's cluster occupancy (sets p.cluster and p.grid).
+cudaError_t attn_prepare(AttnPlan& p);
+cudaError_t attn_launch(const AttnPlan& p, AttnArgs a, const AttnMaps& m, cudaStream_t stream, bool pdl);
 
 // The plan of a standalone launch, built and prepared (attn_prepare) on the first call for each
 // (device, shape) and looked up afterwards, so only that first call does host work and it must come

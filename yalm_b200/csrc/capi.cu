@@ -195,7 +195,11 @@ extern "C" int yb_attention_dev(float* out, const float* q, const uint16_t* k_ca
   a.step = nullptr;
   a.kv_len = kv_len;
   a.max_seq_len = max_seq_len;
-  YB_CK(attn_launch(p, a, static_cast<cudaStream_t>(stream), false));
+  a.cta_slots = LaunchTuning::from_env().attn_cta_slots;
+  AttnMaps m;
+  if (!attn_maps(&m, a.k_cache, a.v_cache, n_kv_heads, max_seq_len, head_dim))
+    return set_error(YB_E_CUDA, "tensor map encoding of the KV cache failed");
+  YB_CK(attn_launch(p, a, m, static_cast<cudaStream_t>(stream), false));
   return 0;
 }
 

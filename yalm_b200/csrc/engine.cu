@@ -173,6 +173,8 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
     if ((rc = dev_alloc(e, &L.v_cache, kvb))) return rc;
     YB_CK(cudaMemset(L.k_cache, 0, kvb));
     YB_CK(cudaMemset(L.v_cache, 0, kvb));
+    if (!attn_maps(&L.attn_maps, L.k_cache, L.v_cache, e->nkv, c.max_seq_len, hd))
+      return set_error(YB_E_CUDA, "tensor map encoding of the KV cache failed");
   }
   if ((rc = ld.finish())) return rc;
   e->upload_bytes = ld.bytes();
@@ -281,9 +283,10 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       a.counters = e->attn_cnt;
       a.step = e->step;
       a.max_seq_len = c.max_seq_len;
+      a.cta_slots = e->tune.attn_cta_slots;
       a.status = e->status_d;
       timeline(&a.trace, &a.trace_stride);
-      YB_CK(attn_launch(e->plan_attn, a, s, true));
+      YB_CK(attn_launch(e->plan_attn, a, L.attn_maps, s, true));
     }
     // ---- wo (+ residual, or partials to peers)
     {
@@ -864,7 +867,8 @@ extern "C" int yb_profile_kernel(yb_engine* e, int which, int iters, float* ms_p
         std::memset(&t, 0, sizeof(t));
         t.q = e->q; t.k_cache = L.k_cache; t.v_cache = L.v_cache; t.out = e->att; t.part = e->attn_part;
         t.counters = e->attn_cnt; t.step = e->step; t.max_seq_len = c.max_seq_len; t.status = e->status_d;
-        YB_CK(attn_launch(e->plan_attn, t, e->stream, true));
+        t.cta_slots = e->tune.attn_cta_slots;
+        YB_CK(attn_launch(e->plan_attn, t, L.attn_maps, e->stream, true));
         return 0;
       }
       case 2:

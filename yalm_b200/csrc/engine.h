@@ -35,6 +35,7 @@ struct LayerBuffers {
   float* rms_ffn = nullptr;
   __half* k_cache = nullptr;  // [kv_heads_l][max_seq_len][head_dim]
   __half* v_cache = nullptr;
+  yb::AttnMaps attn_maps{};   // TMA maps of k_cache / v_cache for the decode attention
 };
 
 // Tensor-parallel exchange region (one device allocation per rank, mapped by every peer).

@@ -499,6 +499,7 @@ LaunchTuning LaunchTuning::from_env() {
         else if (k == "pfq" && v >= 0) t.prefetch_qkv = v != 0;
         else if (k == "pfo" && v >= 0) t.prefetch_wo = v != 0;
         else if (k == "pctr" && v >= 1 && v <= 64) t.persist_claim_ctrs = v;
+        else if (k == "aslots" && v >= 16 && v % 16 == 0) t.attn_cta_slots = v;
       }
       i = j + 1;
     }

@@ -24,9 +24,10 @@ struct LaunchTuning {
   bool prefetch_wo = false;         // graph executor: QKV kernels warm L2 with the layer's Wo
   int persist_static_pct = 100;     // persistent executor: statically split share of each matvec
   int persist_claim_ctrs = 8;       // persistent executor: counters for the dynamically claimed rest
+  int attn_cta_slots = 128;         // decode attention: cache slots per CTA before a kv head splits further
 
-  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2" (read once
-  // per process) for tuning sweeps.
+  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2,aslots=128"
+  // (read once per process) for tuning sweeps.
   static LaunchTuning from_env();
 };
 

@@ -60,7 +60,7 @@ extern "C" int yb_attention_dev_noalloc(float* out, const float* q, const uint16
     return set_error(YB_E_INVALID, "attention scratch of " + std::to_string(need) + " bytes exceeds the " +
                                        std::to_string(kNoAllocScratchBytes) +
                                        "-byte fixed buffer of yb_attention_dev_noalloc (n_heads * "
-                                       "ceil(max_seq_len / 128) * (head_dim + 4) * 4 + n_kv_heads * 4)");
+                                       "min(32, ceil(max_seq_len / 128)) * (head_dim + 2) * 4 + n_kv_heads * 4)");
   AttnPlan p;
   int rc = cached_attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len, &p);
   if (rc) return rc;
@@ -82,6 +82,10 @@ extern "C" int yb_attention_dev_noalloc(float* out, const float* q, const uint16
   a.step = nullptr;
   a.kv_len = kv_len;
   a.max_seq_len = max_seq_len;
-  YB_CK(attn_launch(p, a, s, false));
+  a.cta_slots = LaunchTuning::from_env().attn_cta_slots;
+  AttnMaps m;
+  if (!attn_maps(&m, a.k_cache, a.v_cache, n_kv_heads, max_seq_len, head_dim))
+    return set_error(YB_E_CUDA, "tensor map encoding of the KV cache failed");
+  YB_CK(attn_launch(p, a, m, s, false));
   return 0;
 }

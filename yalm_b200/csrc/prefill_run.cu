@@ -1,8 +1,9 @@
 // yb_prefill: a prompt through the model in one batched pass (tensor-core GEMMs for every matrix,
 // causal attention over the new and the cached slots), replacing the token-by-token prompt loop of
 // yalm's run_completion (src/main.cpp:171-177).  The KV cache ends up as the per-token steps would
-// leave it (to fp16 rounding of the activations); the last token's logits come from the decode
-// classifier kernel.
+// leave it (to fp16 rounding of the activations).  The last token runs as one decode step, so its
+// logits come from the fp32-activation arithmetic of the per-token path: only the cached slots of
+// the earlier prompt tokens carry the batched pass's rounding.
 #include "engine.h"
 #include "prefill.cuh"
 #include "prefill_gemm.cuh"
@@ -64,20 +65,8 @@ static bool batched_ok(const yb_engine* e, int n, int pos0) {
          c.dim % 64 == 0 && e->q_rows % 64 == 0 && e->hid % 64 == 0 && (c.head_dim == 64 || c.head_dim == 128);
 }
 
-extern "C" int yb_prefill(yb_engine* e, const int* tokens, int n, int pos0, float* logits) {
-  if (!e || !tokens || n <= 0 || pos0 < 0) return set_error(YB_E_INVALID, "bad prefill arguments");
-  for (int i = 0; i < n; ++i)
-    if (tokens[i] < 0 || tokens[i] >= e->cfg.vocab_size) return set_error(YB_E_INVALID, "token out of range");
-  if (!batched_ok(e, n, pos0)) {
-    // per-token steps, as yalm's prompt loop runs them
-    for (int i = 0; i < n; ++i) {
-      const bool last = i + 1 == n;
-      int rc = yb_forward(e, tokens[i], pos0 + i, last && logits ? YB_MODE_OUTPUT_LOGITS : YB_MODE_HYDRATE_KV_CACHE,
-                          last ? logits : nullptr);
-      if (rc) return rc;
-    }
-    return yb_sync(e);
-  }
+// The batched pass over tokens[0, n) at positions pos0.. (KV cache only).
+static int prefill_batched(yb_engine* e, const int* tokens, int n, int pos0) {
   YB_CK(cudaSetDevice(e->device));
   int rc = ensure_buffers(e, n);
   if (rc) return rc;
@@ -100,23 +89,26 @@ extern "C" int yb_prefill(yb_engine* e, const int* tokens, int n, int pos0, floa
     if ((rc = gemm(p.xn, L.w13, n, 2 * e->hid, c.dim, kPreSwiGLU, nullptr, p.h, e->hid, s))) return rc;
     if ((rc = gemm(p.h, L.w2, n, c.dim, e->hid, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
   }
-  // the last token's residual stream -> the decode classifier (final RMSNorm + logits)
-  YB_CK(cudaMemcpyAsync(e->x, p.x + (size_t)(n - 1) * c.dim, (size_t)c.dim * 4, cudaMemcpyDeviceToDevice, s));
-  if (logits) {
-    GemvArgs a;
-    std::memset(&a, 0, sizeof(a));
-    a.status = e->status_d;
-    a.eps = c.norm_eps;
-    a.tp_size = 1;
-    a.w = e->wcls;
-    a.ldw = c.dim;
-    a.rows = e->vocab_l;
-    a.cols = c.dim;
-    a.x = e->x;
-    a.norm_w = e->rms_final;
-    a.y = e->logits;
-    YB_CK(gemv_launch(e->plan_cls, a, s, false, 0));
-    YB_CK(cudaMemcpyAsync(logits, e->logits, (size_t)c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
+  return 0;
+}
+
+extern "C" int yb_prefill(yb_engine* e, const int* tokens, int n, int pos0, float* logits) {
+  if (!e || !tokens || n <= 0 || pos0 < 0) return set_error(YB_E_INVALID, "bad prefill arguments");
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= e->cfg.vocab_size) return set_error(YB_E_INVALID, "token out of range");
+  // all but the last token in one batched pass when it covers them, else as yalm's prompt loop
+  // runs them; the last token is one decode step (its logits when asked for)
+  int first = 0;
+  if (batched_ok(e, n - 1, pos0)) {
+    int rc = prefill_batched(e, tokens, n - 1, pos0);
+    if (rc) return rc;
+    first = n - 1;
+  }
+  for (int i = first; i < n; ++i) {
+    const bool last = i + 1 == n;
+    int rc = yb_forward(e, tokens[i], pos0 + i, last && logits ? YB_MODE_OUTPUT_LOGITS : YB_MODE_HYDRATE_KV_CACHE,
+                        last ? logits : nullptr);
+    if (rc) return rc;
   }
   return yb_sync(e);
 }

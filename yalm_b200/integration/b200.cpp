@@ -1,12 +1,13 @@
 // yalm-side binding of the yalm_b200 engine: src/b200.cpp of a yalm checkout.
 //
-// Together with yalm.patch (a `-d b200` device: Device::CUDA_B200, Model::cuda_b200(),
-// InferenceState::cuda_b200(), one branch in Model::forward, src/model.cpp:479-494, and the device
-// name in src/main.cpp) this file is everything yalm needs to run its completion, perplexity and
-// passkey modes on the engine.  It fills the C ABI's structs (include/yalm_b200.h) from yalm's own
-// Config / Block / Model objects before anything is uploaded — the tensor pointers are still the
-// mmap'd .yalm data (src/model.cpp:392-435) — and forwards each Model::forward call to yb_forward,
-// which writes the logits into InferenceState::logits() as yalm's CUDA backends do.
+// Together with yalm.patch (a `-d b200` device: Model::cuda_b200() and a flag that Model::forward,
+// src/model.cpp:479-494, checks first, and the device name in src/main.cpp) this file is everything
+// yalm needs to run its completion, perplexity and passkey modes on the engine.  It fills the C
+// ABI's structs (include/yalm_b200.h) from yalm's own Config / Block / Model objects before anything
+// is uploaded — the tensor pointers are still the mmap'd .yalm data (src/model.cpp:392-435) — and
+// forwards each Model::forward call to yb_forward, which writes the logits into the host buffer
+// InferenceState::logits().  Model and InferenceState stay CPU objects (the engine owns all device
+// memory), so their destructors free only what yalm allocated on the host.
 #include "model.h"
 #include "yalm_b200.h"
 

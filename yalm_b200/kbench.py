@@ -132,7 +132,7 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
     g = torch.Generator(device="cuda").manual_seed(seed)
     msl = kv_len if msl is None else max(msl, kv_len)
     kvbytes = 2 * nkv * msl * hd * 2
-    n = _copies(kvbytes)
+    n = _copies(2 * nkv * kv_len * hd * 2)  # copies enough that the rows read rotate through > 4 x L2
     ks = [torch.randn(nkv, msl, hd, device="cuda", generator=g).half() for _ in range(n)]
     vs = [torch.randn(nkv, msl, hd, device="cuda", generator=g).half() for _ in range(n)]
     q = torch.randn(nh * hd, device="cuda", generator=g)
@@ -144,7 +144,7 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
         _lib.call("yb_attention_dev", _p(out), _p(q), _p(ks[i % n]), _p(vs[i % n]), nh, nkv, hd, msl, kv_len,
                   _p(scratch), stream)
     ms = _time(fn, iters)
-    nbytes = kvbytes + 2 * nh * hd * 4
+    nbytes = 2 * nkv * kv_len * hd * 2 + 2 * nh * hd * 4  # the K / V rows read, q in, out
     return {"kernel": "attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "kv_len": kv_len, "max_seq_len": msl,
             "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n, **_LAST_SPREAD}
 
