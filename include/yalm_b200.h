@@ -263,9 +263,12 @@ int yb_attention_dev_noalloc(float* out, const float* q, const uint16_t* k_cache
 
 /* Batched-prefill tensor-core GEMM on device buffers (no counterpart in yalm, which prefills one
  * token at a time, src/main.cpp:171-177): C[m][n] = sum_k A[m][k] * B[n][k] with A fp16 [M][K],
- * B fp16 [N][K] (a weight matrix as stored), fp32 accumulation; epi 0 stores C into out_f32, 1 adds
- * C to out_f32, 2 writes silu(C[m][2j]) * C[m][2j+1] to out_f16[m][j], 3 stores C as fp16 into
- * out_f16; ldo is the output row stride in elements.  K must be a multiple of 64 and N of 8. */
+ * B fp16 [N][K] (a weight matrix as stored), fp32 accumulation; epi & 3: 0 stores C into out_f32,
+ * 1 adds C to out_f32, 2 writes silu(C[m][2j]) * C[m][2j+1] to out_f16[m][j], 3 stores C as fp16
+ * into out_f16; ldo is the output row stride in elements.  Flags: epi | 4 — A is two planes
+ * [2][M][K], fp16 values and their fp16 remainders, both multiplied into C (fp32-like accuracy from
+ * fp16 tensor cores); epi | 8 (with 2 or 3) — also write each fp16 output's remainder at
+ * out_f16 + M * ldo.  K must be a multiple of 64 and N of 8. */
 int yb_prefill_gemm_dev(float* out_f32, uint16_t* out_f16, const uint16_t* a, const uint16_t* b, int M, int N, int K,
                         int epi, int ldo, void* stream);
 

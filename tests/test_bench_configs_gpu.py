@@ -157,12 +157,13 @@ def test_long_context_3202_prompt_then_decode(gpu, long_context_2layer, prompt_p
     worst = _engine_teacher_forced(m, ids, logits, len(prompt), f"kv_len 3203..3232 ({prompt_path})")
     m.sync()
     # the cache the decode steps read: each value within one fp16 ulp of the reference's plus a
-    # share of its slot's RMS.  The per-token path differs from yalm's only in the order of sums
-    # (yalm's -ffast-math rmsnorm) and in the last bits of the RoPE angles, which a value that is a
-    # difference of two near-equal products magnifies; on the batched path every activation entering
-    # a GEMM is rounded to fp16 (2^-11 relative), which moves each output by about that share of its
-    # row's magnitude, and layer 1 inherits layer 0's attention error over up to 3232 slots.
-    alpha = {"per_token": 2.0 ** -10, "batched": 2.0 ** -7}[prompt_path]
+    # share of its slot's RMS.  Both paths differ from yalm's in the order of sums (yalm's
+    # -ffast-math rmsnorm; the tensor-core GEMMs of the batched path, which take each activation as
+    # an fp16 value plus its fp16 remainder and accumulate to about 2^-16 of the output) and in the
+    # last bits of the RoPE angles, which a value that is a difference of two near-equal products
+    # magnifies; layer 1 also inherits layer 0's attention over up to 3232 slots (measured: at most
+    # 3.3e-3 of the slot RMS, a few fp16 ulps, on the batched path).
+    alpha = {"per_token": 2.0 ** -10, "batched": 2.0 ** -8}[prompt_path]
     for (l, g), (kr, vr) in kv.items():
         k, v = m.read_kv(l, g, 0, 3232)
         for name, got, exp in (("k", k, kr), ("v", v, vr)):
@@ -171,7 +172,8 @@ def test_long_context_3202_prompt_then_decode(gpu, long_context_2layer, prompt_p
             ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(e), 2.0 ** -14))) - 10)
             rms = np.sqrt((e * e).mean(axis=1, keepdims=True))
             rel = (d / rms).max()
-            print(f"{name} layer {l} head {g} ({prompt_path}): max |diff| / slot rms {rel:.2e}, "
+            worst_slot = int(np.unravel_index(np.argmax(d / rms), d.shape)[0])
+            print(f"{name} layer {l} head {g} ({prompt_path}): max |diff| / slot rms {rel:.2e} (slot {worst_slot}), "
                   f"{(d > 0).mean():.4f} of values differ")
             assert np.all(d <= ulp + alpha * rms), (name, l, g, prompt_path, rel)
     assert m.status() == 0

@@ -286,7 +286,7 @@ extern "C" int yb_prefill_attention_dev(uint16_t* out, const float* q, const uin
   using namespace yb;
   if (!out || !q || !k_cache || !v_cache) return set_error(YB_E_INVALID, "null buffer");
   YB_CK(prefill_attention(q, reinterpret_cast<const __half*>(k_cache), reinterpret_cast<const __half*>(v_cache),
-                          reinterpret_cast<__half*>(out), T, pos0, n_heads, n_kv_heads, head_dim, max_seq_len,
+                          reinterpret_cast<__half*>(out), nullptr, T, pos0, n_heads, n_kv_heads, head_dim, max_seq_len,
                           static_cast<cudaStream_t>(stream)));
   return 0;
 }
@@ -294,12 +294,16 @@ extern "C" int yb_prefill_attention_dev(uint16_t* out, const float* q, const uin
 extern "C" int yb_prefill_gemm_dev(float* out_f32, uint16_t* out_f16, const uint16_t* a, const uint16_t* b, int M,
                                    int N, int K, int epi, int ldo, void* stream) {
   using namespace yb;
-  if (epi < kPreStore || epi > kPreStoreF16) return set_error(YB_E_INVALID, "bad epilogue");
+  const int kind = epi & 3;
+  if (epi < 0 || epi > 15 || ((epi & 8) && kind != kPreSwiGLU && kind != kPreStoreF16))
+    return set_error(YB_E_INVALID, "bad epilogue");
   PrefillGemmArgs g{};
   g.M = M;
   g.N = N;
   g.K = K;
-  g.epi = epi;
+  g.epi = kind;
+  g.a_planes = (epi & 4) ? 2 : 1;
+  g.lo_out = (epi & 8) ? 1 : 0;
   g.ldo = ldo;
   g.out_f32 = out_f32;
   g.out_f16 = reinterpret_cast<__half*>(out_f16);

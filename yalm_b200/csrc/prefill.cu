@@ -9,8 +9,17 @@
 namespace yb {
 
 // ---------------------------------------------------------------------------------------- RMSNorm
+// fp32 pair -> fp16 pair at hi[i] and, when lo is set, its fp16 remainder at lo[i] (the two sum to the
+// fp32 values within about 2^-22 relative, for the tensor-core GEMMs that take both as planes).
+__device__ __forceinline__ void store_hilo(__half* hi, __half* lo, size_t i, float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  *reinterpret_cast<__half2*>(hi + i) = h;
+  if (lo) *reinterpret_cast<__half2*>(lo + i) = __floats2half2_rn(a - __low2float(h), b - __high2float(h));
+}
+
 __global__ void __launch_bounds__(256) prefill_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                              __half* __restrict__ xn, int dim, float eps) {
+                                                              __half* __restrict__ xn, __half* __restrict__ xn_lo,
+                                                              int dim, float eps) {
   __shared__ float red[8];
   const float* xr = x + (size_t)blockIdx.x * dim;
   float ss = 0.f;
@@ -25,18 +34,19 @@ __global__ void __launch_bounds__(256) prefill_rmsnorm_kernel(const float* __res
 #pragma unroll
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float scale = 1.0f / sqrtf(tot / (float)dim + eps);
-  __half* o = xn + (size_t)blockIdx.x * dim;
+  const size_t row = (size_t)blockIdx.x * dim;
   for (int i = threadIdx.x * 4; i < dim; i += blockDim.x * 4) {
     const float4 v = *reinterpret_cast<const float4*>(xr + i);
     const float4 g = *reinterpret_cast<const float4*>(w + i);
-    *reinterpret_cast<__half2*>(o + i) = __floats2half2_rn(v.x * scale * g.x, v.y * scale * g.y);
-    *reinterpret_cast<__half2*>(o + i + 2) = __floats2half2_rn(v.z * scale * g.z, v.w * scale * g.w);
+    store_hilo(xn, xn_lo, row + i, v.x * scale * g.x, v.y * scale * g.y);
+    store_hilo(xn, xn_lo, row + i + 2, v.z * scale * g.z, v.w * scale * g.w);
   }
 }
 
-cudaError_t prefill_rmsnorm(const float* x, const float* w, __half* xn, int T, int dim, float eps, cudaStream_t s) {
+cudaError_t prefill_rmsnorm(const float* x, const float* w, __half* xn, __half* xn_lo, int T, int dim, float eps,
+                            cudaStream_t s) {
   if (T <= 0 || dim % 4) return cudaErrorInvalidValue;
-  prefill_rmsnorm_kernel<<<T, 256, 0, s>>>(x, w, xn, dim, eps);
+  prefill_rmsnorm_kernel<<<T, 256, 0, s>>>(x, w, xn, xn_lo, dim, eps);
   return cudaGetLastError();
 }
 
@@ -108,8 +118,8 @@ __host__ __device__ constexpr int pa_row_bytes(int hd) { return hd * 2 + 16; }
 template <int HD, int GQ>
 __global__ void __launch_bounds__(256, 1)
     prefill_attention_kernel(const float* __restrict__ q, const __half* __restrict__ k_cache,
-                             const __half* __restrict__ v_cache, __half* __restrict__ out, int T, int pos0,
-                             int n_heads, int msl) {
+                             const __half* __restrict__ v_cache, __half* __restrict__ out, __half* __restrict__ out_lo,
+                             int T, int pos0, int n_heads, int msl) {
   constexpr int QW = kPaRows / GQ;  // queries per warp
   constexpr int QB = 8 * QW;        // queries per CTA
   constexpr int KS = HD / 16;       // k-steps of S over head_dim
@@ -305,11 +315,10 @@ __global__ void __launch_bounds__(256, 1)
     lt += __shfl_xor_sync(0xffffffffu, lt, 2);
     if (tq[hf] < T) {
       const int r = g4 + 8 * hf;
-      __half* dst = out + (size_t)tq[hf] * q_dim + (size_t)(g * GQ + r % GQ) * HD + 2 * c4;
+      const size_t dst = (size_t)tq[hf] * q_dim + (size_t)(g * GQ + r % GQ) * HD + 2 * c4;
       const float inv = 1.f / lt;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<__half2*>(dst + 8 * nt) = __floats2half2_rn(o[nt][2 * hf] * inv, o[nt][2 * hf + 1] * inv);
+      for (int nt = 0; nt < NT; ++nt) store_hilo(out, out_lo, dst + 8 * nt, o[nt][2 * hf] * inv, o[nt][2 * hf + 1] * inv);
     }
   }
 }
@@ -327,8 +336,9 @@ const void* pick_pa(int gq) {
 }
 }  // namespace
 
-cudaError_t prefill_attention(const float* q, const __half* k_cache, const __half* v_cache, __half* out, int T, int pos0,
-                              int n_heads, int n_kv_heads, int head_dim, int max_seq_len, cudaStream_t s) {
+cudaError_t prefill_attention(const float* q, const __half* k_cache, const __half* v_cache, __half* out, __half* out_lo,
+                              int T, int pos0, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
+                              cudaStream_t s) {
   if (T <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || pos0 + T > max_seq_len) return cudaErrorInvalidValue;
   const int gq = n_heads / n_kv_heads;
   const void* fn = head_dim == 128 ? pick_pa<128>(gq) : head_dim == 64 ? pick_pa<64>(gq) : nullptr;
@@ -338,7 +348,7 @@ cudaError_t prefill_attention(const float* q, const __half* k_cache, const __hal
   if (e != cudaSuccess) return e;
   const int qb = 8 * (kPaRows / gq);
   const dim3 grid((T + qb - 1) / qb, n_kv_heads);
-  void* args[] = {&q, &k_cache, &v_cache, &out, &T, &pos0, &n_heads, &max_seq_len};
+  void* args[] = {&q, &k_cache, &v_cache, &out, &out_lo, &T, &pos0, &n_heads, &max_seq_len};
   return cudaLaunchKernel(fn, grid, dim3(256), args, smem, s);
 }
 

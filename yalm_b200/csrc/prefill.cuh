@@ -9,8 +9,10 @@
 
 namespace yb {
 
-// Row-wise RMSNorm of x fp32 [T][dim] into xn fp16 [T][dim] (yalm src/infer.cpp:136-146).
-cudaError_t prefill_rmsnorm(const float* x, const float* w, __half* xn, int T, int dim, float eps, cudaStream_t s);
+// Row-wise RMSNorm of x fp32 [T][dim] into xn fp16 [T][dim] (yalm src/infer.cpp:136-146); with xn_lo
+// non-null also each value's fp16 remainder there (xn + xn_lo = the fp32 result to ~2^-22).
+cudaError_t prefill_rmsnorm(const float* x, const float* w, __half* xn, __half* xn_lo, int T, int dim, float eps,
+                            cudaStream_t s);
 
 // Per token t (position pos0 + t): clip, interleaved-pair RoPE on q and k, q -> q_out fp32
 // [T][q_rows], k / v -> fp16 cache slot pos0 + t (src/infer.cpp:283-305).  qkv fp32 [T][q+2kv].
@@ -19,8 +21,10 @@ cudaError_t prefill_qkv_post(const float* qkv, int T, int pos0, int q_rows, int 
                              __half* k_cache, __half* v_cache, cudaStream_t s);
 
 // Causal GQA attention of T queries at positions pos0 .. pos0 + T - 1 over cache slots
-// 0 .. pos0 + t (src/infer.cpp:218-250): out fp16 [T][n_heads * head_dim].
-cudaError_t prefill_attention(const float* q, const __half* k_cache, const __half* v_cache, __half* out, int T,
-                              int pos0, int n_heads, int n_kv_heads, int head_dim, int max_seq_len, cudaStream_t s);
+// 0 .. pos0 + t (src/infer.cpp:218-250): out fp16 [T][n_heads * head_dim], and with out_lo non-null
+// each value's fp16 remainder there.
+cudaError_t prefill_attention(const float* q, const __half* k_cache, const __half* v_cache, __half* out, __half* out_lo,
+                              int T, int pos0, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
+                              cudaStream_t s);
 
 }  // namespace yb

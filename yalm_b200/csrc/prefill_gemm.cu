@@ -90,8 +90,37 @@ __device__ __forceinline__ uint32_t pack_h2(float x, float y) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// n fp32 values as fp16 at o (16-byte stores when whole and aligned); with lo set, each value's fp16
+// remainder at the same index of lo.
+template <int NV>
+__device__ __forceinline__ void store_f16(__half* o, __half* lo, const float (&r)[NV], int valid) {
+  if (valid == NV && (reinterpret_cast<uintptr_t>(o) & 15) == 0 && (!lo || (reinterpret_cast<uintptr_t>(lo) & 15) == 0)) {
+#pragma unroll
+    for (int i = 0; i < NV / 8; ++i) {
+      uint32_t h[4], l[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __half2 hh = __floats2half2_rn(r[8 * i + 2 * k], r[8 * i + 2 * k + 1]);
+        h[k] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[k] = pack_h2(r[8 * i + 2 * k] - __low2float(hh), r[8 * i + 2 * k + 1] - __high2float(hh));
+      }
+      reinterpret_cast<uint4*>(o)[i] = make_uint4(h[0], h[1], h[2], h[3]);
+      if (lo) reinterpret_cast<uint4*>(lo)[i] = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      if (i < valid) {
+        const __half h = __float2half_rn(r[i]);
+        o[i] = h;
+        if (lo) lo[i] = __float2half_rn(r[i] - __half2float(h));
+      }
+  }
+}
+
 // Writes 32 accumulator columns (tile columns col .. col + 31) of one row with the fused epilogue.
 __device__ __forceinline__ void epilogue_chunk(const PrefillGemmArgs& a, int row, int col, const float (&v)[32]) {
+  const size_t lo_off = (size_t)a.M * a.ldo;
   if (a.epi == kPreSwiGLU) {
     // (gate, up) column pairs -> silu(gate) * up at column col / 2 + i
     __half* o = a.out_f16 + (size_t)row * a.ldo + col / 2;
@@ -101,28 +130,10 @@ __device__ __forceinline__ void epilogue_chunk(const PrefillGemmArgs& a, int row
       const float g = v[2 * i], u = v[2 * i + 1];
       r[i] = g / (1.0f + expf(-g)) * u;
     }
-    if (col + 32 <= a.N && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-      reinterpret_cast<uint4*>(o)[0] = make_uint4(pack_h2(r[0], r[1]), pack_h2(r[2], r[3]), pack_h2(r[4], r[5]),
-                                                   pack_h2(r[6], r[7]));
-      reinterpret_cast<uint4*>(o)[1] = make_uint4(pack_h2(r[8], r[9]), pack_h2(r[10], r[11]), pack_h2(r[12], r[13]),
-                                                   pack_h2(r[14], r[15]));
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (col + 2 * i + 1 < a.N) o[i] = __float2half_rn(r[i]);
-    }
+    store_f16<16>(o, a.lo_out ? o + lo_off : nullptr, r, min(16, (a.N - col) / 2));
   } else if (a.epi == kPreStoreF16) {
     __half* o = a.out_f16 + (size_t)row * a.ldo + col;
-    if (col + 32 <= a.N && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        reinterpret_cast<uint4*>(o)[i] = make_uint4(pack_h2(v[8 * i], v[8 * i + 1]), pack_h2(v[8 * i + 2], v[8 * i + 3]),
-                                                    pack_h2(v[8 * i + 4], v[8 * i + 5]), pack_h2(v[8 * i + 6], v[8 * i + 7]));
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (col + i < a.N) o[i] = __float2half_rn(v[i]);
-    }
+    store_f16<32>(o, a.lo_out ? o + lo_off : nullptr, v, min(32, a.N - col));
   } else {
     float* o = a.out_f32 + (size_t)row * a.ldo + col;
     if (col + 32 <= a.N && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
@@ -158,6 +169,7 @@ __global__ void __launch_bounds__(kPreThreads, 1)
   const int tiles_m = (a.M + kPreBM - 1) / kPreBM;
   const int n_tiles = tiles_m * ((a.N + kPreBN - 1) / kPreBN);
   const int nk = a.K / kPreBK;
+  const int nkv = nk * (a.a_planes == 2 ? 2 : 1);  // k-blocks per tile over the A planes
   const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
@@ -190,7 +202,10 @@ __global__ void __launch_bounds__(kPreThreads, 1)
       int it = 0;  // k-blocks issued over all tiles of this CTA
       for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += G) {
         const int m0 = (t % tiles_m) * kPreBM, n0 = (t / tiles_m) * kPreBN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kv = 0; kv < nkv; ++kv, ++it) {
+          // k-block kv % nk of A plane kv / nk (rows of plane p start at p * M) against the same
+          // k-block of B
+          const int kb = kv % nk, plane = kv / nk;
           const int s = it % kPreStages;
           if (it >= kPreStages && !mbar_wait(&empty[s], ((it / kPreStages) - 1) & 1, a.status)) {
             *abort_flag = 1;
@@ -198,7 +213,7 @@ __global__ void __launch_bounds__(kPreThreads, 1)
           }
           unsigned char* sa = smem + (size_t)s * kStageBytes;
           mbar_arrive_expect_tx(&full[s], (unsigned)kStageBytes);
-          tma_load_2d(sa, &map_a, kb * kPreBK, m0, &full[s]);
+          tma_load_2d(sa, &map_a, kb * kPreBK, plane * a.M + m0, &full[s]);
           tma_load_2d(sa + kTileABytes, &map_b, kb * kPreBK, n0, &full[s]);
         }
       }
@@ -220,7 +235,7 @@ __global__ void __launch_bounds__(kPreThreads, 1)
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(b * kPreBN);
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = 0; kb < nkv; ++kb, ++it) {
           const int s = it % kPreStages;
           if (!mbar_wait(&full[s], (it / kPreStages) & 1, a.status)) {
             ok = false;
@@ -273,7 +288,7 @@ namespace {
 
 // Row-major fp16 matrix [rows][cols] read in boxes of box_rows x 64 columns, 128-byte swizzle;
 // rows beyond the matrix read as zeros.
-bool make_map(CUtensorMap* m, const __half* base, int rows, int cols, int box_rows) {
+bool make_map(CUtensorMap* m, const __half* base, long long rows, int cols, int box_rows) {
   return tmap_f16_2d_sw128(m, base, rows, cols, kPreBK, box_rows);
 }
 
@@ -284,8 +299,9 @@ cudaError_t prefill_gemm(const __half* A, const __half* B, const PrefillGemmArgs
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15))
     return cudaErrorInvalidValue;
   if ((args.epi == kPreSwiGLU || args.epi == kPreStoreF16) ? !args.out_f16 : !args.out_f32) return cudaErrorInvalidValue;
+  if (args.a_planes != 1 && args.a_planes != 2) return cudaErrorInvalidValue;
   CUtensorMap ma, mb;
-  if (!make_map(&ma, A, args.M, args.K, kPreBM) || !make_map(&mb, B, args.N, args.K, kPreBN))
+  if (!make_map(&ma, A, (long long)args.M * args.a_planes, args.K, kPreBM) || !make_map(&mb, B, args.N, args.K, kPreBN))
     return cudaErrorInvalidValue;
   const size_t smem = (size_t)kPreStages * kStageBytes + 1024;
   static bool attr_set[64] = {};  // per device

@@ -32,10 +32,14 @@ struct PrefillGemmArgs {
   float* out_f32;
   __half* out_f16;
   unsigned* status;
+  int a_planes;     // 1, or 2: A is [2][M][K], an fp16 value plane and its fp16 remainder plane,
+                    // both multiplied by B into the same accumulator (about fp32 accuracy)
+  int lo_out;       // fp16 epilogues: also write each value's fp16 remainder at out_f16 + M * ldo
 };
 
-// Host: builds the two tensor maps and launches (A: M x K, box 128 x 64; B: N x K, box 256 x 64).
-// Returns a CUDA error code (cudaErrorInvalidValue for unsupported shapes: K % 64, N % 8).
+// Host: builds the two tensor maps and launches (A: a_planes * M x K, box 128 x 64; B: N x K, box
+// 256 x 64).  Returns a CUDA error code (cudaErrorInvalidValue for unsupported shapes: K % 64,
+// N % 8).
 cudaError_t prefill_gemm(const __half* A, const __half* B, const PrefillGemmArgs& args, cudaStream_t stream);
 
 }  // namespace yb

@@ -1,9 +1,9 @@
 // yb_prefill: a prompt through the model in one batched pass (tensor-core GEMMs for every matrix,
 // causal attention over the new and the cached slots), replacing the token-by-token prompt loop of
 // yalm's run_completion (src/main.cpp:171-177).  The KV cache ends up as the per-token steps would
-// leave it (to fp16 rounding of the activations).  The last token runs as one decode step, so its
-// logits come from the fp32-activation arithmetic of the per-token path: only the cached slots of
-// the earlier prompt tokens carry the batched pass's rounding.
+// leave it: every fp16 activation entering a GEMM goes in as two planes, the fp16 value and its fp16
+// remainder, so the products keep about 22 bits as the per-token path's fp32 dot products do.  The
+// last token runs as one decode step (yb_forward), whose logits the caller receives.
 #include "engine.h"
 #include "prefill.cuh"
 #include "prefill_gemm.cuh"
@@ -30,12 +30,13 @@ int ensure_buffers(yb_engine* e, int T) {
   p = yb_engine::Prefill{};
   const size_t cap = (size_t)((T + 127) / 128 * 128);
   const size_t qkv_rows = (size_t)e->q_rows + 2 * e->kv_rows;
+  // the GEMMs' fp16 inputs hold two planes each: values and their fp16 remainders
   YB_CK(cudaMalloc(&p.x, cap * c.dim * 4));
-  YB_CK(cudaMalloc(&p.xn, cap * c.dim * 2));
+  YB_CK(cudaMalloc(&p.xn, 2 * cap * c.dim * 2));
   YB_CK(cudaMalloc(&p.qkv, cap * qkv_rows * 4));
   YB_CK(cudaMalloc(&p.q, cap * e->q_rows * 4));
-  YB_CK(cudaMalloc(&p.att, cap * e->q_rows * 2));
-  YB_CK(cudaMalloc(&p.h, cap * e->hid * 2));
+  YB_CK(cudaMalloc(&p.att, 2 * cap * e->q_rows * 2));
+  YB_CK(cudaMalloc(&p.h, 2 * cap * e->hid * 2));
   YB_CK(cudaMalloc(&p.tokens, cap * 4));
   p.cap = (int)cap;
   return 0;
@@ -52,6 +53,8 @@ int gemm(const __half* A, const __half* B, int M, int N, int K, int epi, float* 
   g.out_f32 = of;
   g.out_f16 = oh;
   g.status = nullptr;
+  g.a_planes = 2;          // A: values + remainders, [2][M][K]
+  g.lo_out = oh ? 1 : 0;   // fp16 outputs feed the next GEMM as two planes too
   YB_CK(prefill_gemm(A, B, g, s));
   return 0;
 }
@@ -79,13 +82,14 @@ static int prefill_batched(yb_engine* e, const int* tokens, int n, int pos0) {
   YB_CK(cudaGetLastError());
   for (int l = 0; l < c.n_layers; ++l) {
     LayerBuffers& L = e->layers[l];
-    YB_CK(prefill_rmsnorm(p.x, L.rms_att, p.xn, n, c.dim, c.norm_eps, s));
+    YB_CK(prefill_rmsnorm(p.x, L.rms_att, p.xn, p.xn + (size_t)n * c.dim, n, c.dim, c.norm_eps, s));
     if ((rc = gemm(p.xn, L.wqkv, n, qkv_rows, c.dim, kPreStore, p.qkv, nullptr, qkv_rows, s))) return rc;
     YB_CK(prefill_qkv_post(p.qkv, n, pos0, e->q_rows, e->kv_rows, c.head_dim, c.rotary_dim, c.max_seq_len, c.qkv_clip,
                            e->inv_freq, p.q, L.k_cache, L.v_cache, s));
-    YB_CK(prefill_attention(p.q, L.k_cache, L.v_cache, p.att, n, pos0, e->nh, e->nkv, c.head_dim, c.max_seq_len, s));
+    YB_CK(prefill_attention(p.q, L.k_cache, L.v_cache, p.att, p.att + (size_t)n * e->q_rows, n, pos0, e->nh, e->nkv,
+                            c.head_dim, c.max_seq_len, s));
     if ((rc = gemm(p.att, L.wo, n, c.dim, e->q_rows, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
-    YB_CK(prefill_rmsnorm(p.x, L.rms_ffn, p.xn, n, c.dim, c.norm_eps, s));
+    YB_CK(prefill_rmsnorm(p.x, L.rms_ffn, p.xn, p.xn + (size_t)n * c.dim, n, c.dim, c.norm_eps, s));
     if ((rc = gemm(p.xn, L.w13, n, 2 * e->hid, c.dim, kPreSwiGLU, nullptr, p.h, e->hid, s))) return rc;
     if ((rc = gemm(p.h, L.w2, n, c.dim, e->hid, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
   }
