@@ -209,6 +209,8 @@ def run_reference(args):
     steps = d["step_s"][args.warmup:]
     t = sum(steps)
     v = len(steps) / t
+    ref_gpu = reference_gpu(path, context, n + args.warmup, args.warmup, prompt, d["tokens"]) \
+        if args.config != "llama-70b" and not args.no_reference_gpu else None
     sample = (f"{len(steps)} timed decode tokens at positions {PROMPT_LEN + args.warmup}..{PROMPT_LEN + args.warmup + len(steps) - 1} "
               f"(+{args.warmup} warm-up) of the full {args.config} model after the workload's {PROMPT_LEN}-token "
               f"prompt, yalm -d cpu code path (Model::forward) via oracle/_ref/ref_decode")
@@ -224,9 +226,42 @@ def run_reference(args):
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
                          "sample": sample},
         "greedy_ids": d["tokens"],
+        "reference_gpu": ref_gpu,
         "gpu_launches": 0,
     }))
     return 0
+
+
+def reference_gpu(path, context, n_decode, warmup, prompt, cpu_ids):
+    """yalm's own GPU backends on this box, beside the reference arm's CPU figure (not its value):
+    oracle/_ref/ref_decode_gpu (yalm's sources built for sm_100a) with -d cuda (the CUDA-graph
+    backend, src/infer.cu:1274-1378) and -d cuda-coop (the cooperative kernel, src/coop.cu:378-415)
+    on the same checkpoint, prompt and positions, wall clock per decode step (each step syncs for
+    its logits, as run_completion's loop does); and oracle/_ref/ref_kernels: yalm's per-layer decode
+    kernels alone with the launch shapes of Block::_block_cuda (src/infer.cu:891-1072), CUDA events
+    over 64 launches rotating over more than 4 x L2 of weights / cache."""
+    import oracle
+    if not (os.path.exists(oracle.REF_BIN_GPU) and os.path.exists(oracle.REF_KERNELS)):
+        return {"unavailable": "oracle/_ref/ref_decode_gpu or ref_kernels not built"}
+    out = {}
+    for dev in ("cuda", "cuda-coop"):
+        r = subprocess.run([oracle.REF_BIN_GPU, path, str(context), str(n_decode), "1", "-d", dev] +
+                           [str(t) for t in prompt], capture_output=True, text=True, timeout=900)
+        line = [l for l in r.stdout.splitlines() if l.startswith("{")]
+        if r.returncode != 0 or not line:
+            out[dev] = {"failed": (r.stderr or r.stdout)[-300:]}
+            continue
+        rec = json.loads(line[-1])
+        st = rec["step_s"][warmup:]
+        out[dev] = {"tok_s": round(len(st) / sum(st), 2), "ms_per_step": round(1000 * sum(st) / len(st), 4),
+                    "steps": len(st), "greedy_ids_equal_cpu": rec["tokens"] == list(cpu_ids)}
+    r = subprocess.run([oracle.REF_KERNELS, "64", str(PROMPT_LEN + DECODE_LEN // 2), "3232"], capture_output=True,
+                       text=True, timeout=600)
+    line = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    out["kernels"] = json.loads(line[-1])["kernels"] if r.returncode == 0 and line else {"failed": r.stderr[-300:]}
+    out["how"] = ("yalm's -d cuda / -d cuda-coop decode loop (oracle/_ref/ref_decode_gpu, built from its sources for "
+                  "sm_100a) and its per-layer kernels alone (oracle/_ref/ref_kernels), same box")
+    return out
 
 
 def main():
@@ -240,6 +275,8 @@ def main():
                     help="cap on the reference arm's timed steps (default: the workload's decode positions)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="reference arm: skip timing yalm's own GPU backends beside its CPU path")
     ap.add_argument("--no-profile", action="store_true")
     ap.add_argument("--no-long-context", action="store_true", help="skip the config-3 (3202-token prefill) phase")
     ap.add_argument("--dtype", default="fp16", choices=["fp16", "fp8"],
@@ -269,6 +306,8 @@ def main():
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
             dist.barrier()  # the communicator exists after the first collective
 
+    tp_check = tp_parity(world, rank, local, dist)
+    log(f"[bench] rank {rank}: tensor-parallel check {tp_check}")
     path = model_file(args.config, rank, world, dist, args.dtype)
     context = 8192 if args.config == "llama-70b" else 0
     y = YALMData(path)
@@ -450,6 +489,10 @@ def main():
                             "how": "free-running greedy ids after the workload's prompt: yb_forward_sample (this arm's "
                                    "e2e loop) vs yalm's CPU path (ref_decode, argmax, sampler.cpp:27-38)"}
 
+    tp_ex = None
+    if world > 1 and executor == "graph":
+        m.close()
+        tp_ex = tp_exchange(args.config, path, context, world, rank, local, dist)
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -489,6 +532,8 @@ def main():
             "graph_kernels_us": kernels,
             "cpu_baseline": cpu,
             "greedy_match": greedy_match,
+            "tp_check": tp_check,
+            "tp_exchange_us": tp_ex,
             "long_context": long_ctx,
             "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,
@@ -499,6 +544,101 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def tp_parity(world, rank, local, dist):
+    """The tensor-parallel check the bench runs first at every N: the small 8-kv-head checkpoint of
+    tests/golden/kv8_golden.npz (made by tests/golden/make_golden.py from yalm's CPU path), split
+    over the N ranks as the benchmark model is; forced steps compared with the golden logits
+    (max-abs <= 2e-2, cosine >= 0.9999), free-running greedy ids with the golden ones (up to the first
+    step whose golden top-2 gap is under 2e-3), and every rank's logits bit-identical to rank 0's."""
+    import hashlib
+    import tempfile
+    from yalm_b200 import InferenceMode, InferenceState, Model, YALMData, synth
+    gold = dict(np.load(os.path.join(ROOT, "tests", "golden", "kv8_golden.npz")))
+    shape = synth.shape_with("tiny", **json.loads(str(gold["shape_json"])))
+    path = os.path.join(tempfile.gettempdir(), f"yalm_kv8_seed{int(gold['seed'])}.yalm")
+    if rank == 0:
+        synth.write_yalm(path, shape, seed=int(gold["seed"]))
+    if world > 1:
+        dist.barrier()
+    m = Model(YALMData(path)).cuda(local, rank, world)
+    if world > 1:
+        def ag(b):
+            out = [None] * world
+            dist.all_gather_object(out, b)
+            return out
+        m.tp_join(ag)
+    s = InferenceState(m.config)
+    h = hashlib.sha256()
+    steps = [int(x) for x in gold["logit_steps"]]
+    worst, ok = 0.0, True
+    for pos, tok in enumerate(gold["forced"]):
+        m.forward(s, int(tok), pos, InferenceMode.OUTPUT_LOGITS)
+        lg = s.logits()
+        h.update(lg.tobytes())
+        if pos in steps:
+            exp = gold["logits"][steps.index(pos)]
+            d = float(np.abs(lg - exp).max())
+            c = float(lg @ exp / (np.linalg.norm(lg) * np.linalg.norm(exp)))
+            worst = max(worst, d)
+            ok = ok and d <= 2e-2 and c >= 0.9999
+    prompt = [int(t) for t in gold["prompt"]]
+    for pos, tok in enumerate(prompt):
+        m.forward(s, tok, pos, InferenceMode.OUTPUT_LOGITS if pos + 1 == len(prompt) else InferenceMode.HYDRATE_KV_CACHE)
+    greedy = []
+    for i in range(len(gold["greedy"])):
+        tok = int(np.argmax(s.logits()))
+        greedy.append(tok)
+        h.update(s.logits().tobytes())
+        m.forward(s, tok, len(prompt) + i)
+    n_sure = next((i for i, gp in enumerate(gold["greedy_gap"]) if gp < 2e-3), len(greedy))
+    greedy_ok = greedy[:n_sure] == [int(t) for t in gold["greedy"][:n_sure]]
+    status = m.status()
+    m.close()
+    digests = [h.hexdigest()]
+    if world > 1:
+        digests = [None] * world
+        dist.all_gather_object(digests, h.hexdigest())
+    return {"tp_parity_ok": bool(ok and greedy_ok and status == 0), "logits_bit_identical_across_ranks":
+            len(set(digests)) == 1, "ranks": world, "worst_logit_max_abs": round(worst, 6),
+            "logit_steps_compared": len(steps), "greedy_steps_equal": n_sure if greedy_ok else 0,
+            "fixture": "tests/golden/kv8_golden.npz (dim 1024, 16 q / 8 kv heads, 4 layers; yalm's CPU path)"}
+
+
+def tp_exchange(config, path, context, world, rank, local, dist):
+    """Exchange latency of the tensor-parallel all-reduces, from the engine's timeline (YB_TRACE=1):
+    a second engine of the benchmark model runs a few decode steps; per exchange point, the reader
+    kernel's last CTA to hold the all-reduced input minus this rank's last writer CTA (wo, w2
+    epilogue end), median over the layers, max over the ranks."""
+    import torch
+    from yalm_b200 import InferenceMode, Model, YALMData
+    from yalm_b200 import timeline
+    os.environ["YB_TRACE"] = "1"
+    try:
+        m = Model(YALMData(path), context=context).cuda(local, rank, world)
+    finally:
+        del os.environ["YB_TRACE"]
+
+    def ag(b):
+        out = [None] * world
+        dist.all_gather_object(out, b)
+        return out
+    m.tp_join(ag)
+    for i in range(8):
+        m.forward_async(100 + i, PROMPT_LEN + i, InferenceMode.OUTPUT_LOGITS)
+    m.sync()
+    tr = timeline.read(m.engine)
+    ex = timeline.exchange_latency(tr, m.config.n_layers)
+    ph = timeline.layer_phases(tr, m.config.n_layers, timeline.w2_panels_of(m.config, world))
+    m.close()
+    t = torch.tensor([ex["wo_to_gateup_us"] or 0.0, ex["w2_to_qkv_us"] or 0.0], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"wo_to_gateup_us": round(float(t[0]), 2), "w2_to_qkv_us": round(float(t[1]), 2),
+            "per_exchange_us": round(float(t.mean()), 2), "exchanges_per_step": 2 * m.config.n_layers,
+            "rank0_layer_phases_us": ph,
+            "how": "engine timeline (YB_TRACE=1, %globaltimer): reader kernel's last all-reduced CTA minus this "
+                   "rank's last writer epilogue, median over layers, max over ranks"}
 
 
 LONG_PREFILL, LONG_DECODE = 3202, 30

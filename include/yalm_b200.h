@@ -187,6 +187,12 @@ int yb_tp_export(yb_engine* e, void* blob, size_t blob_bytes, size_t* used);
 int yb_tp_import(yb_engine* e, const void* blobs, size_t blob_stride);
 size_t yb_tp_blob_bytes(void);
 
+/* The slices yb_create uploads for rank tp_rank of tp_size (host arithmetic, no device needed), as
+ * element ranges [begin, end): out8 = {Wq rows / Wo columns, Wk and Wv rows, W1 / W3 rows and W2
+ * columns, classifier rows}.  The embedding and the norm weights are replicated.  No counterpart
+ * in yalm, which runs on one GPU (src/model.cpp:442-443). */
+int yb_tp_shard(const yb_config* cfg, int tp_rank, int tp_size, long long* out8);
+
 /* ---------------------------------------------------------------- kernel-level entry points
  * Counterparts of yalm's test hooks (src/model.h:340-374: matmul_cuda, mha_cuda, ffn_cuda), with
  * the same argument meaning: host arrays in, host arrays out, synchronous.  They allocate device

@@ -79,6 +79,7 @@ def kv8_shape():
 
 def generate_kv8(path: str):
     """kv8_golden.npz:
+      shape_json, seed  the checkpoint (shape overrides of the tiny config, synthetic seed)
       forced          24 token ids (default_rng(8)), each step in OUTPUT_LOGITS mode from position 0
       logit_steps     steps whose logits are stored;  logits  float32 [len(logit_steps), 4096]
       prompt          16 token ids; greedy: 16 greedy ids after it;  greedy_gap: top-1 minus top-2
@@ -108,7 +109,9 @@ def generate_kv8(path: str):
     y = YALMData(path)
     crc = {n: zlib.crc32(bytes(y.buf[t.offset:t.offset + min(4096, t.size)])) for n, t in y.tensors.items()}
     names = sorted(crc)
-    return dict(forced=forced, logit_steps=np.array(KV8_LOGIT_STEPS, np.int32), logits=np.stack(keep).astype(np.float32),
+    import json
+    return dict(shape_json=np.array(json.dumps(KV8_SHAPE, sort_keys=True)), seed=np.array(KV8_SEED, np.int32),
+                forced=forced, logit_steps=np.array(KV8_LOGIT_STEPS, np.int32), logits=np.stack(keep).astype(np.float32),
                 prompt=prompt, greedy=np.array(greedy, np.int32), greedy_gap=np.array(gaps, np.float32),
                 weight_crc_names=np.array(names), weight_crc=np.array([crc[n] for n in names], np.uint32))
 

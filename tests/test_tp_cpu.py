@@ -1,5 +1,6 @@
 """The tensor-parallel partition on CPU ranks (gloo, world sizes 2 and 4): each rank runs the decode math
-of its shard (yalm_b200.tp.shard — the slices the engine uploads), the wo / w2 partial sums are
+of its shard (yalm_b200.tp.shard — the engine's own slice table, read through the C ABI's
+yb_tp_shard, host arithmetic only), the wo / w2 partial sums are
 exchanged and added in rank order as the engine's kernels do, the logits are gathered, and the
 result must equal the unsharded forward pass."""
 import os
@@ -133,16 +134,14 @@ def test_tensor_parallel_partition_gloo(tiny_yalm, world, kv_heads):
 def test_partition_covers_every_row_once_and_rejects_uneven_worlds():
     """The slices of all ranks tile Wq / Wk / Wv / W1 / W3 / classifier rows exactly once, in rank
     order; a world size that would split a GQA group or the hidden units unevenly is refused."""
-    from yalm_b200 import synth
+    from yalm_b200 import Config, YalmB200Error, synth
     from yalm_b200.tp import shard
 
-    class C:
-        pass
     for name in ("mistral-7b", "llama-70b"):
         shp = synth.SHAPES[name]
-        c = C()
-        c.n_heads, c.n_kv_heads, c.head_dim = shp.n_heads, shp.n_kv_heads, shp.head_dim
-        c.hidden_dim, c.vocab_size = shp.hidden_dim, shp.vocab_size
+        c = Config(dim=shp.dim, hidden_dim=shp.hidden_dim, head_dim=shp.head_dim, n_layers=shp.n_layers,
+                   n_heads=shp.n_heads, n_kv_heads=shp.n_kv_heads, vocab_size=shp.vocab_size,
+                   max_seq_len=4096, rope_theta=shp.rope_theta, rotary_dim=shp.head_dim, act=1)
         for world in (1, 2, 4, 8):
             parts = [shard(c, r, world) for r in range(world)]
             for field, total in (("q_rows", c.n_heads * c.head_dim), ("kv_rows", c.n_kv_heads * c.head_dim),
@@ -154,7 +153,7 @@ def test_partition_covers_every_row_once_and_rejects_uneven_worlds():
             gq = c.n_heads // c.n_kv_heads
             for p in parts:
                 assert p.q_rows.start == p.kv_rows.start * gq and p.q_rows.stop == p.kv_rows.stop * gq
-        with pytest.raises(ValueError):
+        with pytest.raises(YalmB200Error):
             shard(c, 0, 16)  # 8 kv heads cannot go to 16 ranks
-        with pytest.raises(ValueError):
+        with pytest.raises(YalmB200Error):
             shard(c, 0, 3)

@@ -72,6 +72,7 @@ _SIGS = {
     "yb_tp_export": (_I, [_P, _P, _S, ctypes.POINTER(_S)]),
     "yb_tp_import": (_I, [_P, _P, _S]),
     "yb_tp_blob_bytes": (_S, []),
+    "yb_tp_shard": (_I, [_P, _I, _I, _P]),
     "yb_matmul": (_I, [_P, _P, _P, _I, _I]),
     "yb_mha": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I]),
     "yb_ffn": (_I, [_P, _P, _P, _P, _P, _I, _I, _I]),

@@ -109,9 +109,19 @@ int check_config(const yb_config* c, int tp_size) {
 
 }  // namespace
 
+// The slices of every tensor-parallel matrix that rank r of P holds (yb_tp_shard exports the same
+// table): query heads (rows of Wq, columns of Wo) and kv heads (rows of Wk, Wv) in blocks of whole
+// heads, so each GQA group stays on one rank; hidden units (rows of W1, W3, columns of W2); and
+// classifier rows.  Element index ranges [begin, end).
+static ShardTable shard_table(const yb_config& c, int r, int P) {
+  const long long qr = (long long)(c.n_heads / P) * c.head_dim, kr = (long long)(c.n_kv_heads / P) * c.head_dim;
+  const long long h = c.hidden_dim / P, v = c.vocab_size / P;
+  return ShardTable{r * qr, (r + 1) * qr, r * kr, (r + 1) * kr, r * h, (r + 1) * h, r * v, (r + 1) * v};
+}
+
 static int upload_weights(yb_engine* e, const yb_weights* w) {
   const yb_config& c = e->cfg;
-  const int r = e->tp_rank;
+  const ShardTable& st = e->shard;
   const size_t dim = c.dim, hd = c.head_dim;
   const size_t q_dim = (size_t)c.n_heads * hd;
   const size_t es = e->esz;  // bytes per weight
@@ -127,7 +137,7 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
     e->wcls = e->emb;  // tied embeddings
   } else {
     if ((rc = dev_alloc(e, &e->wcls, (size_t)e->vocab_l * dim * es))) return rc;
-    if ((rc = ld.contiguous(e->wcls, bytes(w->wcls) + (size_t)r * e->vocab_l * dim * es, (size_t)e->vocab_l * dim * es)))
+    if ((rc = ld.contiguous(e->wcls, bytes(w->wcls) + (size_t)st.v0 * dim * es, (size_t)e->vocab_l * dim * es)))
       return rc;
   }
   e->layers.resize(c.n_layers);
@@ -143,9 +153,9 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
     // [Wq rows of this rank's heads; Wk rows; Wv rows]
     const size_t qr = e->q_rows, kr = e->kv_rows;
     if ((rc = dev_alloc(e, &L.wqkv, (qr + 2 * kr) * dim * es))) return rc;
-    const unsigned char* wq = bytes(w->wq[l]) + (size_t)r * qr * dim * es;
-    const unsigned char* wk = bytes(w->wk[l]) + (size_t)r * kr * dim * es;
-    const unsigned char* wv = bytes(w->wv[l]) + (size_t)r * kr * dim * es;
+    const unsigned char* wq = bytes(w->wq[l]) + (size_t)st.q0 * dim * es;
+    const unsigned char* wk = bytes(w->wk[l]) + (size_t)st.kv0 * dim * es;
+    const unsigned char* wv = bytes(w->wv[l]) + (size_t)st.kv0 * dim * es;
     const size_t rb = dim * es;  // bytes per row of a dim-wide matrix
     rc = ld.rows(L.wqkv, qr + 2 * kr, rb, [=](size_t i) -> const void* {
       return i < qr ? wq + i * rb : i < qr + kr ? wk + (i - qr) * rb : wv + (i - qr - kr) * rb;
@@ -153,18 +163,18 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
     if (rc) return rc;
     // Wo columns of this rank's heads
     if ((rc = dev_alloc(e, &L.wo, dim * qr * es))) return rc;
-    const unsigned char* wo = bytes(w->wo[l]) + (size_t)r * qr * es;
+    const unsigned char* wo = bytes(w->wo[l]) + (size_t)st.q0 * es;
     if ((rc = ld.rows(L.wo, dim, qr * es, [=](size_t i) -> const void* { return wo + i * q_dim * es; }))) return rc;
     // W1 / W3 rows of this rank's hidden slice, interleaved (row 2i = W1 row i, 2i+1 = W3 row i)
     const size_t h = e->hid;
     if ((rc = dev_alloc(e, &L.w13, 2 * h * dim * es))) return rc;
-    const unsigned char* w1 = bytes(w->w1[l]) + (size_t)r * h * rb;
-    const unsigned char* w3 = bytes(w->w3[l]) + (size_t)r * h * rb;
+    const unsigned char* w1 = bytes(w->w1[l]) + (size_t)st.h0 * rb;
+    const unsigned char* w3 = bytes(w->w3[l]) + (size_t)st.h0 * rb;
     rc = ld.rows(L.w13, 2 * h, rb, [=](size_t i) -> const void* { return ((i & 1) ? w3 : w1) + (i >> 1) * rb; });
     if (rc) return rc;
     // W2 columns of the hidden slice
     if ((rc = dev_alloc(e, &L.w2, dim * h * es))) return rc;
-    const unsigned char* w2 = bytes(w->w2[l]) + (size_t)r * h * es;
+    const unsigned char* w2 = bytes(w->w2[l]) + (size_t)st.h0 * es;
     const size_t hid_row = (size_t)c.hidden_dim * es;
     if ((rc = ld.rows(L.w2, dim, h * es, [=](size_t i) -> const void* { return w2 + i * hid_row; }))) return rc;
     // KV cache, zero-initialised like yalm's (src/model.cpp:203-204)
@@ -442,12 +452,13 @@ static int engine_init(yb_engine* e, const yb_config* cfg, const yb_weights* w, 
   e->tp_rank = tp_rank;
   e->tp_size = tp_size;
   const yb_config& c = e->cfg;
+  e->shard = shard_table(c, tp_rank, tp_size);
   e->nh = c.n_heads / tp_size;
   e->nkv = c.n_kv_heads / tp_size;
-  e->q_rows = e->nh * c.head_dim;
-  e->kv_rows = e->nkv * c.head_dim;
-  e->hid = c.hidden_dim / tp_size;
-  e->vocab_l = c.vocab_size / tp_size;
+  e->q_rows = (int)(e->shard.q1 - e->shard.q0);
+  e->kv_rows = (int)(e->shard.kv1 - e->shard.kv0);
+  e->hid = (int)(e->shard.h1 - e->shard.h0);
+  e->vocab_l = (int)(e->shard.v1 - e->shard.v0);
   YB_CK(cudaSetDevice(device));
   YB_CK(cudaDeviceGetAttribute(&e->n_sms, cudaDevAttrMultiProcessorCount, device));
   YB_CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
@@ -778,6 +789,17 @@ extern "C" int yb_read_kv(yb_engine* e, int layer, int kv_head, int slot0, int n
   const size_t off = ((size_t)kv_head * e->cfg.max_seq_len + slot0) * hd;
   if (k_out) YB_CK(cudaMemcpy(k_out, e->layers[layer].k_cache + off, (size_t)n * hd * 2, cudaMemcpyDeviceToHost));
   if (v_out) YB_CK(cudaMemcpy(v_out, e->layers[layer].v_cache + off, (size_t)n * hd * 2, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+extern "C" int yb_tp_shard(const yb_config* cfg, int tp_rank, int tp_size, long long* out8) {
+  if (!cfg || !out8) return set_error(YB_E_INVALID, "null argument");
+  int rc = check_config(cfg, tp_size);
+  if (rc) return rc;
+  if (tp_rank < 0 || tp_rank >= tp_size) return set_error(YB_E_INVALID, "tp_rank out of range");
+  const ShardTable st = shard_table(*cfg, tp_rank, tp_size);
+  const long long v[8] = {st.q0, st.q1, st.kv0, st.kv1, st.h0, st.h1, st.v0, st.v1};
+  for (int i = 0; i < 8; ++i) out8[i] = v[i];
   return 0;
 }
 

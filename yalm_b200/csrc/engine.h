@@ -26,6 +26,14 @@ const std::string& last_error();
       return ::yb::set_error(YB_E_CUDA, std::string(#x) + " failed: " + cudaGetErrorString(_e));    \
   } while (0)
 
+// Element ranges [begin, end) of the tensor-parallel slices one rank holds (engine.cu shard_table).
+struct ShardTable {
+  long long q0, q1;    // rows of Wq, columns of Wo
+  long long kv0, kv1;  // rows of Wk, Wv
+  long long h0, h1;    // rows of W1 / W3, columns of W2
+  long long v0, v1;    // classifier rows
+};
+
 struct LayerBuffers {
   __half* wqkv = nullptr;   // [q_rows + 2 kv_rows, dim]: this rank's Wq, Wk, Wv rows
   __half* wo = nullptr;     // [dim, q_rows]: this rank's Wo columns
@@ -112,6 +120,7 @@ struct yb_engine {
   yb::GemvPlan plan_qkv{}, plan_wo{}, plan_gu{}, plan_w2{}, plan_cls{};
   yb::GemvPlan plan_qkv_tp{};  // tensor parallel: QKV of layers >= 1 (adds the previous w2 partials)
   int w2_panels = 1;
+  yb::ShardTable shard{};
   yb::AttnPlan plan_attn{};
 
   // executor: per-step CUDA graph of kernels (false) or one persistent cooperative kernel (true)

@@ -14,7 +14,7 @@ namespace yb {
 // WT: weight type, 0 = fp16, 1 = fp8 E5M2 (the top byte of an fp16).  A 16-byte chunk of a row holds
 // EPC = 8 or 16 weights; thread t owns the chunks t, t + NT, ... and the matching EPC values of x.
 template <int NW, int KPT, int RT, int EPI, int IN, int WT>
-__global__ void __launch_bounds__((NW + 1) * 32, 2) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvArgs a) {
   constexpr bool NORM = IN >= 1;
   constexpr bool TPIN = IN == 2;
   constexpr int EPC = WT ? 16 : 8;  // weights (and x values) per 16-byte chunk
@@ -414,7 +414,7 @@ namespace {
 
 template <int KPT, int RT, int EPI, int IN, int WT>
 const void* pick4() {
-  return reinterpret_cast<const void*>(&gemv_kernel<kGemvWarps, KPT, RT, EPI, IN, WT>);
+  return reinterpret_cast<const void*>(&yb_stream_matvec<kGemvWarps, KPT, RT, EPI, IN, WT>);
 }
 // Instantiated combinations: residual epilogues never normalise their input; the tensor-parallel
 // logits epilogue always does; pair epilogues (gate/up, QKV) need at least two rows per stage; the

@@ -1,17 +1,20 @@
-"""Tensor-parallel partition of one decoder layer (host-side description).
+"""Tensor-parallel partition of one decoder layer, as the engine holds it.
 
-The engine (yb_create with tp_size > 1, yalm_b200/csrc/engine.cu upload_weights) gives rank r of P:
-  Wq rows of query heads [r*nh/P, (r+1)*nh/P)         Wk, Wv rows of kv heads [r*nkv/P, (r+1)*nkv/P)
-  Wo columns of the same query heads                  (row-parallel: partial sums over heads)
-  W1, W3 rows of hidden units [r*H/P, (r+1)*H/P)      W2 columns of the same hidden units (partials)
-  classifier rows of vocabulary [r*V/P, (r+1)*V/P)    embedding and norm weights replicated
-so each GQA group stays on one rank, attention needs no exchange, and the only exchanges per layer
-are the sums of the wo and w2 partials (added in rank order 0..P-1 on every rank) plus one gather
-of the logits per output step.  This module states the same slices for tests and tools.
+yb_create with tp_size > 1 gives rank r of P (yalm_b200/csrc/engine.cu, shard_table): Wq rows of a
+block of whole query heads and the Wo columns of the same heads (row-parallel: partial sums over
+heads); Wk, Wv rows of a block of whole kv heads, so each GQA group stays on one rank; W1, W3 rows of
+a block of hidden units and the W2 columns of the same units (partial sums); a block of classifier
+rows; the embedding and the norm weights replicated.  The only exchanges per layer are the sums of
+the wo and w2 partials (added in rank order 0..P-1 on every rank) plus one gather of the logits per
+output step.  shard() reads the engine's own table through the C ABI (yb_tp_shard: host
+arithmetic, no GPU needed), so tests check the slices the engine uploads.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
+
+from . import _lib
 
 
 @dataclass(frozen=True)
@@ -23,14 +26,11 @@ class Shard:
 
 
 def shard(config, rank: int, world: int) -> Shard:
-    c = config
-    if c.n_kv_heads % world or c.hidden_dim % (8 * world) or c.vocab_size % world:
-        raise ValueError("world size must divide n_kv_heads, hidden_dim / 8 and vocab_size")
-    nh, nkv = c.n_heads // world, c.n_kv_heads // world
-    hd = c.head_dim
-    h = c.hidden_dim // world
-    v = c.vocab_size // world
-    return Shard(q_rows=slice(rank * nh * hd, (rank + 1) * nh * hd),
-                 kv_rows=slice(rank * nkv * hd, (rank + 1) * nkv * hd),
-                 hidden=slice(rank * h, (rank + 1) * h),
-                 vocab=slice(rank * v, (rank + 1) * v))
+    """Rank `rank` of `world`'s slices (yb_tp_shard); raises YalmB200Error for a world size the
+    engine refuses (it must divide n_kv_heads, vocab_size and hidden_dim / 8)."""
+    cfg = config.to_c()
+    out = (ctypes.c_longlong * 8)()
+    _lib.call("yb_tp_shard", ctypes.byref(cfg), int(rank), int(world), out)
+    v = list(out)
+    return Shard(q_rows=slice(v[0], v[1]), kv_rows=slice(v[2], v[3]), hidden=slice(v[4], v[5]),
+                 vocab=slice(v[6], v[7]))
