@@ -152,9 +152,9 @@ int yb_executor(yb_engine* e);
  *    gate/up, w2; then the classifier in logits mode): for the matvecs j = 0 entry, 1 input vector
  *    loaded, 2 tensor-parallel all-reduce done (before 1), 3 last weight stage consumed, 4 epilogue
  *    done;
- *    for attention (row = blockIdx.y * gridDim.x + blockIdx.x) 0 entry, 1 inputs ready, 2 first
- *    K/V sub-chunk staged, 5 scores done, 6 V pass done, 3 slice done, 4 exit.  Rows beyond a
- *    kernel's grid stay 0. */
+ *    for attention (row = blockIdx.y * gridDim.x + blockIdx.x) 0 entry, 7 early K/V copies
+ *    issued, 1 inputs ready, 2 first K/V stage landed, 5 slots folded, 6 warp weights formed,
+ *    3 CTA record written, 4 exit.  Rows beyond a kernel's grid stay 0. */
 int yb_trace_read(yb_engine* e, unsigned long long* out, size_t n, int* grid, int* events);
 
 /* Status word the kernels of the last step wrote (0 = healthy; bit 0 TMA-stage wait timed out,
@@ -245,6 +245,9 @@ int yb_qkv_dev(float* q_out, uint16_t* k_cache, uint16_t* v_cache, const float* 
 int yb_attention_dev(float* out, const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int n_heads,
                      int n_kv_heads, int head_dim, int max_seq_len, int kv_len, void* scratch_dev, void* stream);
 size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
+/* Diagnostics: the launch yb_attention_dev uses on the current device for this shape,
+ * out4 = {CTAs per cluster, clusters per kv head, CTAs in the grid, dynamic shared memory bytes}. */
+int yb_attention_plan_info(int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int* out4);
 
 /* No counterpart in the yalm reference (it allocates with cudaMalloc wherever it needs memory).
  * yb_attention_dev for callers that must not allocate device memory when they call it — for

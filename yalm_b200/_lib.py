@@ -81,6 +81,7 @@ _SIGS = {
     "yb_qkv_dev": (_I, [_P, _P, _P, _P, _P, _P, _F, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P]),
     "yb_attention_dev": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "yb_attention_scratch_bytes": (_S, [_I, _I, _I, _I]),
+    "yb_attention_plan_info": (_I, [_I, _I, _I, _I, _P]),
     "yb_attention_dev_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "yb_num_sms": (_I, []),
     "yb_profile_kernel": (_I, [_P, _I, _I, ctypes.POINTER(_F)]),

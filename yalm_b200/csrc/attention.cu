@@ -290,6 +290,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive_expect_tx_s(early_s + 8 * c, c < n_early ? STAGE : 0u);
         if (c < n_early) load(h0, c, c, early_s + 8 * c);
       }
+      timeline_stamp(tr, a.trace_stride, 7);
     }
     __syncwarp();
     // waits (bounded) for every early copy to have landed
@@ -461,6 +462,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     named_sync(1, 256);
+    if (threadIdx.x == 0) timeline_stamp(tr, a.trace_stride, 6);
     for (int e = threadIdx.x; e < GQ * HD; e += 256) {
       const int h = e / HD, d = e % HD;
       float O = 0.f;

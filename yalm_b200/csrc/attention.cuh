@@ -23,8 +23,9 @@ struct AttnArgs {
   int cta_slots;          // slots per CTA before a kv head's cache splits over more CTAs (0: 128)
   unsigned* status;
   // optional timeline (null = off): per CTA c = blockIdx.y * gridDim.x + blockIdx.x,
-  // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 1 inputs ready, 2 first stage landed,
-  // 5 slots folded (thread 0), 3 CTA record written, 4 exit (CTAs of idle clusters stamp only 0)
+  // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 7 early copies issued, 1 inputs
+  // ready, 2 first stage landed, 5 slots folded, 6 warp weights formed, 3 record written, 4 exit
+  // (CTAs without slots stamp only 0, 7 and 1)
   unsigned long long* trace;
   int trace_stride;
 };

@@ -176,6 +176,18 @@ extern "C" size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int he
   return (p.part_floats * 4 + 255) / 256 * 256 + (size_t)n_kv_heads * 4;
 }
 
+extern "C" int yb_attention_plan_info(int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int* out4) {
+  if (!out4) return set_error(YB_E_INVALID, "null argument");
+  AttnPlan p;
+  int rc = cached_attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len, &p);
+  if (rc) return rc;
+  out4[0] = p.cluster;
+  out4[1] = (int)p.grid.x / p.cluster;
+  out4[2] = (int)(p.grid.x * p.grid.y);
+  out4[3] = (int)p.smem;
+  return 0;
+}
+
 extern "C" int yb_attention_dev(float* out, const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
                                 int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int kv_len,
                                 void* scratch_dev, void* stream) {

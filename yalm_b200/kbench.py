@@ -144,9 +144,12 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
         _lib.call("yb_attention_dev", _p(out), _p(q), _p(ks[i % n]), _p(vs[i % n]), nh, nkv, hd, msl, kv_len,
                   _p(scratch), stream)
     ms = _time(fn, iters)
+    info = (ctypes.c_int * 4)()
+    _lib.call("yb_attention_plan_info", nh, nkv, hd, msl, info)
     nbytes = 2 * nkv * kv_len * hd * 2 + 2 * nh * hd * 4  # the K / V rows read, q in, out
     return {"kernel": "attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "kv_len": kv_len, "max_seq_len": msl,
-            "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n, **_LAST_SPREAD}
+            "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n,
+            "cluster": info[0], "clusters_per_kv_head": info[1], "ctas": info[2], **_LAST_SPREAD}
 
 
 def bench_prefill_attention(nh, nkv, hd, T, iters, seed=0):

@@ -26,10 +26,12 @@ import numpy as np
 from . import _lib
 
 # stamps per kernel (yb_trace_read): matvecs 0 entry, 1 input loaded, 2 tensor-parallel all-reduce
-# done, 3 last weight stage consumed, 4 epilogue done; attention 0 entry, 1 inputs ready, 2 first
-# chunk staged, 5 slots folded, 3 record written, 4 exit
+# done, 3 last weight stage consumed, 4 epilogue done; attention 0 entry, 7 early copies issued,
+# 1 inputs ready, 2 first chunk staged, 5 slots folded, 6 warp weights formed, 3 record written,
+# 4 exit
 MATVEC = {"entry": 0, "input": 1, "allreduce": 2, "last_stage": 3, "epilogue": 4}
-ATTN = {"entry": 0, "ready": 1, "first_chunk": 2, "folded": 5, "record": 3, "exit": 4}
+ATTN = {"entry": 0, "early_issued": 7, "ready": 1, "first_chunk": 2, "folded": 5, "weights": 6, "record": 3,
+        "exit": 4}
 
 
 def read(engine) -> np.ndarray:
