@@ -246,8 +246,9 @@ int yb_attention_dev(float* out, const float* q, const uint16_t* k_cache, const 
                      int n_kv_heads, int head_dim, int max_seq_len, int kv_len, void* scratch_dev, void* stream);
 size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);
 /* Diagnostics: the launch yb_attention_dev uses on the current device for this shape,
- * out4 = {CTAs per cluster, clusters per kv head, CTAs in the grid, dynamic shared memory bytes}. */
-int yb_attention_plan_info(int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int* out4);
+ * out20 = {CTAs per cluster, clusters per kv head, CTAs in the grid, dynamic shared memory bytes,
+ * then for clusters of 1..16 CTAs the number the device holds at once}. */
+int yb_attention_plan_info(int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int* out20);
 
 /* No counterpart in the yalm reference (it allocates with cudaMalloc wherever it needs memory).
  * yb_attention_dev for callers that must not allocate device memory when they call it — for
@@ -257,7 +258,7 @@ int yb_attention_plan_info(int n_heads, int n_kv_heads, int head_dim, int max_se
  * YB_ATTENTION_NOALLOC_SCRATCH_BYTES array inside this library's device memory, which every GPU that
  * loads the library holds until the process exits.  Nothing is allocated or freed by the call.
  *  - Limit: yb_attention_scratch_bytes(n_heads, n_kv_heads, head_dim, max_seq_len) must not exceed
- *    YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4 MiB: e.g. 32 heads of 128 at max_seq_len 30720); larger
+ *    YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4 MiB: every shape of up to 256 heads of 128 fits); larger
  *    shapes return YB_E_INVALID with the sizes in yb_last_error().
  *  - The first call on each device looks up the array's device address (cudaGetSymbolAddress with
  *    that device current), and the first call for each shape on a device sets up its launch (a

@@ -167,15 +167,16 @@ def test_noalloc_attention_size_limit_checked_on_the_host():
     L = _lib.lib()
     limit = 4 << 20
     p = ctypes.c_void_p(16)
-    # 256 heads of 128 over 32 kv heads need more than 4 MiB of cluster records
-    assert L.yb_attention_scratch_bytes(256, 32, 128, 4096) > limit
+    # 512 heads of 128 over 64 kv heads need more than 4 MiB of cluster records
+    assert L.yb_attention_scratch_bytes(512, 64, 128, 4096) > limit
+    assert L.yb_attention_scratch_bytes(256, 32, 128, 32768) <= limit
     assert L.yb_attention_scratch_bytes(32, 8, 128, 4096) <= limit
     assert L.yb_attention_scratch_bytes(64, 8, 128, 32768) <= limit
-    rc = L.yb_attention_dev_noalloc(p, p, p, p, 256, 32, 128, 4096, 100, None)
+    rc = L.yb_attention_dev_noalloc(p, p, p, p, 512, 64, 128, 4096, 100, None)
     assert rc == _lib.YB_E_INVALID
     msg = _lib.last_error()
     assert "exceeds" in msg and str(limit) in msg
-    assert str(L.yb_attention_scratch_bytes(256, 32, 128, 4096)) in msg  # the size the shape needs
+    assert str(L.yb_attention_scratch_bytes(512, 64, 128, 4096)) in msg  # the size the shape needs
     src = open(_lib.HEADER).read()
     assert "#define YB_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)" in src
 

@@ -58,7 +58,7 @@ def _oracle(q, k, v, nh, nkv, hd, msl, kv_len):
 
 @pytest.mark.parametrize("nh,nkv,hd,msl,kv_len", [(32, 8, 128, 4096, 3232), (8, 2, 64, 1024, 65),
                                                   (32, 8, 128, 4096, 1), (64, 8, 128, 8192, 1152),
-                                                  (8, 2, 128, 8192, 6000)])
+                                                  (8, 2, 128, 8192, 6000), (4, 1, 128, 32768, 30000)])
 def test_noalloc_attention_matches_allocating_entry_point(gpu, nh, nkv, hd, msl, kv_len):
     q, k, v = _inputs(nh, nkv, hd, msl, kv_len + nh)
     exp = _allocating(q, k, v, nh, nkv, hd, msl, kv_len)
@@ -75,7 +75,7 @@ def test_noalloc_attention_shape_changes_reuse_the_array(gpu):
     the array: B's cluster records take more of it than A's, so the place of A's merge counters lies
     inside B's records and holds B's data when A runs again.  Each call must clear what it needs and
     give the allocating entry point's result."""
-    shapes = [(8, 2, 128, 4096, 3000), (16, 2, 128, 8192, 8000), (8, 2, 128, 4096, 3000)]
+    shapes = [(8, 2, 128, 32768, 20000), (16, 2, 128, 32768, 30000), (8, 2, 128, 32768, 20000)]
     sizes = [_lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl) for nh, nkv, hd, msl, _ in shapes]
     assert sizes[1] > sizes[0]
     for i, (nh, nkv, hd, msl, kv_len) in enumerate(shapes):
@@ -87,8 +87,8 @@ def test_noalloc_attention_shape_changes_reuse_the_array(gpu):
 
 def test_noalloc_attention_rejects_oversized_shapes(gpu):
     import torch
-    # needs 32 kv heads * 32 clusters * 8 heads * (128 + 2) floats * 4 bytes of records > 4 MiB
-    nh, nkv, hd, msl = 256, 32, 128, 4096
+    # needs 64 kv heads * 31 clusters * 8 heads * (128 + 2) floats * 4 bytes of records > 4 MiB
+    nh, nkv, hd, msl = 512, 64, 128, 4096
     assert _lib.lib().yb_attention_scratch_bytes(nh, nkv, hd, msl) > (4 << 20)
     q = torch.zeros(nh * hd, device="cuda")
     kv = torch.zeros(1, dtype=torch.float16, device="cuda")

@@ -4,10 +4,11 @@
 // yalm computes, per query head h with kv group g = h / (n_heads / n_kv_heads):
 //   s_t = q_h . k_t / sqrt(head_dim),  p = softmax(s[0..kv_len)),  out_h = sum_t p_t v_t
 // (src/infer.cpp:218-250; the CUDA kernel attn_fused, src/infer.cu:625-667, runs one CTA per q head
-// and reads each K/V head once per q head).  Here a cluster of C CTAs (C = 16 where the GPU can
-// hold n_kv_heads such clusters at once) serves the GQ query heads of one kv head, so K/V bytes
-// cross HBM once per kv head; the cache is split over as many of the cluster's CTAs as it has
-// 128-slot portions, CTA r taking the r-th equal slice (a multiple of 16 slots):
+// and reads each K/V head once per q head).  Here a cluster of C CTAs (C <= 16, sized by
+// attn_prepare so that the kv heads' clusters fill the SMs at once) serves the GQ query heads of one
+// kv head, so K/V bytes cross HBM once per kv head; the cache is split over as many of the
+// cluster's CTAs as it has 128-slot portions, CTA r taking the r-th equal slice (a multiple of 16
+// slots):
 //
 //   * a producer warp streams the slice through a ring of 64-slot stages with 2-D TMA (tensor maps
 //     over the [kv_heads * max_seq_len][head_dim] caches, 64 x 64 boxes with the 128-byte swizzle,
@@ -43,6 +44,7 @@ constexpr int kAttnStages = 4;
 constexpr int kAttnMaxCluster = 16;
 constexpr int kAttnCtaSlots = 128;    // slots per CTA before a kv head's cache splits further
 constexpr int kAttnMaxClusters = 32;  // clusters per kv head
+constexpr int kAttnClusterSlots = 1024;  // slots per CTA of one cluster before more clusters share a kv head
 constexpr int kAttnBox = 64 * 128;    // one 64-row x 128-byte swizzled box
 
 // ---------------------------------------------------------------- cluster helpers
@@ -240,14 +242,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
 
   // A cache of len slots is shared by ceil(len / cta_slots) CTAs at most: by c_eff CTAs of one
-  // cluster, or by all C CTAs of each of n_cl > 1 clusters, each taking an equal slice (a multiple of
-  // 16 slots): this CTA's is [t0, t1), possibly empty.  Clusters cl >= n_cl have nothing to do;
+  // cluster, or, when the CTAs of one cluster would hold more than cluster_slots slots each, by all C
+  // CTAs of each of n_cl > 1 clusters; each takes an equal slice (a multiple of 16 slots): this
+  // CTA's is [t0, t1), possibly empty.  Clusters cl >= n_cl have nothing to do;
   // with one active CTA (single) it writes the outputs itself and no cluster barrier runs.
   const int n_clusters = (int)gridDim.x / C;
   const int cta_slots = a.cta_slots > 0 ? a.cta_slots : kAttnCtaSlots;
-  auto slice = [C, rank, cl, n_clusters, cta_slots](int len, int& t0_, int& t1_, int& ncl_, int& ceff_) {
+  const int cluster_slots = a.cluster_slots > 0 ? a.cluster_slots : kAttnClusterSlots;
+  auto slice = [C, rank, cl, n_clusters, cta_slots, cluster_slots](int len, int& t0_, int& t1_, int& ncl_,
+                                                                   int& ceff_) {
     const int want = max(1, (len + cta_slots - 1) / cta_slots);
-    ncl_ = min(n_clusters, (want + C - 1) / C);
+    ncl_ = min(n_clusters, max(1, (len + C * cluster_slots - 1) / (C * cluster_slots)));
     ceff_ = ncl_ > 1 ? C : min(C, want);
     const int ns = ncl_ * ceff_;
     const int ch = ((len + ns - 1) / ns + 15) / 16 * 16;
@@ -551,20 +556,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     __syncthreads();
     if (s_last) {
+      // Every record of the kv head (contiguous in the scratch) into the CTA's idle stage ring in one
+      // pass of independent 8-byte loads, then the merge from shared memory: one round trip to L2
+      // for the records instead of one per dependent read.
       const float* recs = a.part + (size_t)g * n_clusters * GQ * (HD + 2);
+      float* rs = reinterpret_cast<float*>(smem);  // [n_cl][GQ][HD + 2]
+      const int n2 = n_cl * GQ * (HD + 2) / 2;
+      constexpr int U = 8;
+      for (int i0 = (int)threadIdx.x; i0 < n2; i0 += U * kAttnThreads) {
+        float2 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = i0 + u * kAttnThreads;
+          v[u] = i < n2 ? __ldcg(reinterpret_cast<const float2*>(recs) + i) : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = i0 + u * kAttnThreads;
+          if (i < n2) reinterpret_cast<float2*>(rs)[i] = v[u];
+        }
+      }
+      __syncthreads();
       if (threadIdx.x < GQ) {
         const int h = threadIdx.x;
         float M = -INFINITY;
-#pragma unroll 4
-        for (int q = 0; q < n_cl; ++q) M = fmaxf(M, __ldcg(recs + ((size_t)q * GQ + h) * (HD + 2) + HD));
+        for (int q = 0; q < n_cl; ++q) M = fmaxf(M, rs[(q * GQ + h) * (HD + 2) + HD]);
         float L = 0.f;
-#pragma unroll 4
         for (int q = 0; q < n_cl; ++q) {
-          const float* r = recs + ((size_t)q * GQ + h) * (HD + 2);
-          const float mq = __ldcg(r + HD);
-          const float w = mq > -INFINITY ? expf(mq - M) : 0.f;
+          const float* r = rs + (q * GQ + h) * (HD + 2);
+          const float w = r[HD] > -INFINITY ? expf(r[HD] - M) : 0.f;
           sw[q * GQ + h] = w;
-          L = fmaf(w, __ldcg(r + HD + 1), L);
+          L = fmaf(w, r[HD + 1], L);
         }
         ml[h] = L;
       }
@@ -572,11 +594,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int e = threadIdx.x; e < GQ * HD; e += kAttnThreads) {
         const int h = e / HD, d = e % HD;
         float O = 0.f;
-#pragma unroll 4
-        for (int q = 0; q < n_cl; ++q) {
-          const float w = sw[q * GQ + h];
-          if (w != 0.f) O = fmaf(w, __ldcg(recs + ((size_t)q * GQ + h) * (HD + 2) + d), O);
-        }
+        for (int q = 0; q < n_cl; ++q) O = fmaf(sw[q * GQ + h], rs[(q * GQ + h) * (HD + 2) + d], O);
         a.out[(size_t)g * GQ * HD + e] = O / ml[h];
       }
       if (threadIdx.x == 0) a.counters[g] = 0u;  // ready for the next launch
@@ -611,11 +629,13 @@ AttnPlan attn_plan(int n_heads, int n_kv_heads, int head_dim, int max_seq_len) {
   if (!p.fn) return p;
   p.smem = head_dim == 128 ? attn_smem_bytes(128, gq) : attn_smem_bytes(64, gq);
   // Until attn_prepare sizes it for the device: one cluster of 16 per kv head.  The scratch for the
-  // merge over clusters is sized for any device: at most kAttnMaxClusters clusters of a kv head,
-  // and no more than one per kAttnCtaSlots slots of the context.
+  // merge over clusters is sized for any device: at most kAttnMaxClusters clusters of a kv head, no
+  // more than one per kAttnCtaSlots slots of the context, and no more records than the stage ring
+  // of the merging CTA holds.
   p.cluster = kAttnMaxCluster;
   p.grid = dim3(p.cluster, n_kv_heads);
-  p.s_max = std::min(kAttnMaxClusters, (max_seq_len + kAttnCtaSlots - 1) / kAttnCtaSlots);
+  const int ring_records = (int)(kAttnStages * attn_stage_region(head_dim) / 4 / ((size_t)gq * (head_dim + 2)));
+  p.s_max = std::min({kAttnMaxClusters, (max_seq_len + kAttnCtaSlots - 1) / kAttnCtaSlots, ring_records});
   p.part_floats = (size_t)n_kv_heads * p.s_max * gq * (head_dim + 2);
   p.max_seq_len = max_seq_len;
   p.ok = p.smem <= 227 * 1024;
@@ -642,18 +662,35 @@ cudaError_t attn_prepare(AttnPlan& p) {
     cfg.numAttrs = 1;
     return cudaOccupancyMaxActiveClusters(n, p.fn, &cfg);
   };
-  // the largest power-of-two cluster (<= 16 CTAs) of which the GPU holds one per kv head at once,
-  // then as many clusters per kv head as still run at once (long caches of few kv heads)
-  int c = kAttnMaxCluster, n = 0;
-  for (;; c >>= 1) {
+  // The largest cluster (1..16 CTAs, any size: the merge does not need a power of two) of which the
+  // GPU holds one per kv head at once: the kv heads run in one wave and merge through distributed
+  // shared memory only.  A cluster lies inside one GPC, so on a B200 (148 SMs) seven clusters of 16
+  // fit at once but eleven of 10.  Only where that leaves most SMs idle (few kv heads, a
+  // tensor-parallel rank's) does a kv head get more clusters, as many as still run at once and the
+  // context can fill at cluster_slots slots per CTA; the kernel then takes the extra ones only for
+  // caches that long, since their merge goes through global scratch.
+  const LaunchTuning tune = LaunchTuning::from_env();
+  int dev = 0, n_sms = 148;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  int best_c = 1;
+  for (int c = kAttnMaxCluster; c >= 1; --c) {
+    int n = 0;
     if ((e = max_clusters(c, &n)) != cudaSuccess) return e;
-    if (n >= n_kv || c == 1) break;
+    p.max_active[c - 1] = n;
+    if (best_c == 1 && n >= n_kv) best_c = c;
   }
-  int s = std::max(1, n / n_kv);
-  s = std::min(s, std::max(1, (p.max_seq_len + c * kAttnCtaSlots - 1) / (c * kAttnCtaSlots)));
-  s = std::min(s, p.s_max);
-  p.cluster = c;
-  p.grid = dim3(c * s, n_kv);
+  int best_s = 1;
+  if (2 * best_c * n_kv <= n_sms) {
+    const int cs = std::max(16, tune.attn_cluster_slots);
+    best_s = std::max(1, p.max_active[best_c - 1] / n_kv);
+    best_s = std::min(best_s, std::max(1, (p.max_seq_len + best_c * cs - 1) / (best_c * cs)));
+    best_s = std::min(best_s, p.s_max);
+  }
+  if (tune.attn_cluster > 0) best_c = std::min(tune.attn_cluster, kAttnMaxCluster);
+  if (tune.attn_clusters_per_head > 0) best_s = std::min(tune.attn_clusters_per_head, p.s_max);
+  p.cluster = best_c;
+  p.grid = dim3(best_c * best_s, n_kv);
   return cudaSuccess;
 }
 

@@ -21,6 +21,8 @@ struct AttnArgs {
   int kv_len;             // ... else from here
   int max_seq_len;
   int cta_slots;          // slots per CTA before a kv head's cache splits over more CTAs (0: 128)
+  int cluster_slots;      // slots per CTA of one cluster before the cache takes more clusters of the
+                          // kv head, where the grid has them (0: 1024)
   unsigned* status;
   // optional timeline (null = off): per CTA c = blockIdx.y * gridDim.x + blockIdx.x,
   // trace[c * trace_stride + j] = %globaltimer at j = 0 entry, 7 early copies issued, 1 inputs
@@ -39,6 +41,7 @@ struct AttnPlan {
   int max_seq_len;
   size_t smem;
   size_t part_floats;  // scratch floats for the merge over clusters, valid for any device
+  int max_active[16];  // attn_prepare: clusters of 1..16 CTAs the device holds at once
 };
 
 // TMA tensor maps of one layer's K and V caches: [n_kv_heads * max_seq_len][head_dim] fp16 read in

@@ -176,15 +176,16 @@ extern "C" size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int he
   return (p.part_floats * 4 + 255) / 256 * 256 + (size_t)n_kv_heads * 4;
 }
 
-extern "C" int yb_attention_plan_info(int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int* out4) {
-  if (!out4) return set_error(YB_E_INVALID, "null argument");
+extern "C" int yb_attention_plan_info(int n_heads, int n_kv_heads, int head_dim, int max_seq_len, int* out20) {
+  if (!out20) return set_error(YB_E_INVALID, "null argument");
   AttnPlan p;
   int rc = cached_attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len, &p);
   if (rc) return rc;
-  out4[0] = p.cluster;
-  out4[1] = (int)p.grid.x / p.cluster;
-  out4[2] = (int)(p.grid.x * p.grid.y);
-  out4[3] = (int)p.smem;
+  out20[0] = p.cluster;
+  out20[1] = (int)p.grid.x / p.cluster;
+  out20[2] = (int)(p.grid.x * p.grid.y);
+  out20[3] = (int)p.smem;
+  for (int c = 0; c < 16; ++c) out20[4 + c] = p.max_active[c];
   return 0;
 }
 
@@ -208,6 +209,7 @@ extern "C" int yb_attention_dev(float* out, const float* q, const uint16_t* k_ca
   a.kv_len = kv_len;
   a.max_seq_len = max_seq_len;
   a.cta_slots = LaunchTuning::from_env().attn_cta_slots;
+  a.cluster_slots = LaunchTuning::from_env().attn_cluster_slots;
   AttnMaps m;
   if (!attn_maps(&m, a.k_cache, a.v_cache, n_kv_heads, max_seq_len, head_dim))
     return set_error(YB_E_CUDA, "tensor map encoding of the KV cache failed");

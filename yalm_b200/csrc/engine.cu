@@ -294,6 +294,7 @@ int record_step(yb_engine* e, int mode, const StepArgs& sa) {
       a.step = e->step;
       a.max_seq_len = c.max_seq_len;
       a.cta_slots = e->tune.attn_cta_slots;
+      a.cluster_slots = e->tune.attn_cluster_slots;
       a.status = e->status_d;
       timeline(&a.trace, &a.trace_stride);
       YB_CK(attn_launch(e->plan_attn, a, L.attn_maps, s, true));
@@ -890,6 +891,7 @@ extern "C" int yb_profile_kernel(yb_engine* e, int which, int iters, float* ms_p
         t.q = e->q; t.k_cache = L.k_cache; t.v_cache = L.v_cache; t.out = e->att; t.part = e->attn_part;
         t.counters = e->attn_cnt; t.step = e->step; t.max_seq_len = c.max_seq_len; t.status = e->status_d;
         t.cta_slots = e->tune.attn_cta_slots;
+        t.cluster_slots = e->tune.attn_cluster_slots;
         YB_CK(attn_launch(e->plan_attn, t, L.attn_maps, e->stream, true));
         return 0;
       }

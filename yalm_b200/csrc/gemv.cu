@@ -500,6 +500,9 @@ LaunchTuning LaunchTuning::from_env() {
         else if (k == "pfo" && v >= 0) t.prefetch_wo = v != 0;
         else if (k == "pctr" && v >= 1 && v <= 64) t.persist_claim_ctrs = v;
         else if (k == "aslots" && v >= 16 && v % 16 == 0) t.attn_cta_slots = v;
+        else if (k == "acslots" && v >= 16 && v % 16 == 0) t.attn_cluster_slots = v;
+        else if (k == "acl" && v >= 0 && v <= 16) t.attn_cluster = v;
+        else if (k == "acs" && v >= 0 && v <= 32) t.attn_clusters_per_head = v;
       }
       i = j + 1;
     }

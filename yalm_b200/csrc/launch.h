@@ -25,8 +25,11 @@ struct LaunchTuning {
   int persist_static_pct = 100;     // persistent executor: statically split share of each matvec
   int persist_claim_ctrs = 8;       // persistent executor: counters for the dynamically claimed rest
   int attn_cta_slots = 128;         // decode attention: cache slots per CTA before a kv head splits further
+  int attn_cluster_slots = 1024;    // decode attention: slots per CTA of one cluster before a kv head takes more clusters
+  int attn_cluster = 0;             // decode attention: CTAs per cluster (0: chosen by attn_prepare)
+  int attn_clusters_per_head = 0;   // decode attention: clusters per kv head (0: chosen by attn_prepare)
 
-  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2,aslots=128"
+  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2,aslots=128,acslots=1024,acl=0,acs=0"
   // (read once per process) for tuning sweeps.
   static LaunchTuning from_env();
 };

@@ -59,8 +59,8 @@ extern "C" int yb_attention_dev_noalloc(float* out, const float* q, const uint16
   if (need > kNoAllocScratchBytes)
     return set_error(YB_E_INVALID, "attention scratch of " + std::to_string(need) + " bytes exceeds the " +
                                        std::to_string(kNoAllocScratchBytes) +
-                                       "-byte fixed buffer of yb_attention_dev_noalloc (n_heads * "
-                                       "min(32, ceil(max_seq_len / 128)) * (head_dim + 2) * 4 + n_kv_heads * 4)");
+                                       "-byte fixed buffer of yb_attention_dev_noalloc (n_heads * (head_dim + 2) * 4 per cluster "
+                                       "of a kv head, up to min(32, ceil(max_seq_len / 128)) clusters, + n_kv_heads * 4)");
   AttnPlan p;
   int rc = cached_attn_plan(n_heads, n_kv_heads, head_dim, max_seq_len, &p);
   if (rc) return rc;
@@ -83,6 +83,7 @@ extern "C" int yb_attention_dev_noalloc(float* out, const float* q, const uint16
   a.kv_len = kv_len;
   a.max_seq_len = max_seq_len;
   a.cta_slots = LaunchTuning::from_env().attn_cta_slots;
+  a.cluster_slots = LaunchTuning::from_env().attn_cluster_slots;
   AttnMaps m;
   if (!attn_maps(&m, a.k_cache, a.v_cache, n_kv_heads, max_seq_len, head_dim))
     return set_error(YB_E_CUDA, "tensor map encoding of the KV cache failed");

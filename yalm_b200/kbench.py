@@ -144,12 +144,13 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
         _lib.call("yb_attention_dev", _p(out), _p(q), _p(ks[i % n]), _p(vs[i % n]), nh, nkv, hd, msl, kv_len,
                   _p(scratch), stream)
     ms = _time(fn, iters)
-    info = (ctypes.c_int * 4)()
+    info = (ctypes.c_int * 20)()
     _lib.call("yb_attention_plan_info", nh, nkv, hd, msl, info)
     nbytes = 2 * nkv * kv_len * hd * 2 + 2 * nh * hd * 4  # the K / V rows read, q in, out
     return {"kernel": "attention", "n_heads": nh, "n_kv_heads": nkv, "head_dim": hd, "kv_len": kv_len, "max_seq_len": msl,
             "us": round(ms * 1000, 2), "gbs": round(nbytes / (ms / 1000) / 1e9, 1), "bytes": nbytes, "copies": n,
-            "cluster": info[0], "clusters_per_kv_head": info[1], "ctas": info[2], **_LAST_SPREAD}
+            "cluster": info[0], "clusters_per_kv_head": info[1], "ctas": info[2],
+            "max_active_clusters": list(info[4:20]), **_LAST_SPREAD}
 
 
 def bench_prefill_attention(nh, nkv, hd, T, iters, seed=0):
@@ -216,6 +217,7 @@ def main(argv=None):
     ap.add_argument("--quick", action="store_true", help="one shape per kernel (for profiler captures)")
     ap.add_argument("--kv-lens", default="", help="attention: comma-separated kv_len values")
     ap.add_argument("--msl", type=int, default=0, help="attention: cache capacity (default: kv_len)")
+    ap.add_argument("--heads", default="32,8", help="attention: n_heads,n_kv_heads (head_dim 128)")
     ap.add_argument("--tokens", default="", help="prefill_attention, prefill: comma-separated prompt lengths")
     ap.add_argument("--warm", type=int, default=3, help="untimed launches per case before the timed ones")
     args = ap.parse_args(argv)
@@ -236,8 +238,9 @@ def main(argv=None):
         lens = [4096] if args.quick else [128, 1024, 4096, 16384, 32768]
         if args.kv_lens:
             lens = [int(v) for v in args.kv_lens.split(",")]
+        nh, nkv = (int(v) for v in args.heads.split(","))
         for kv in lens:
-            rows.append(bench_attention(32, 8, 128, kv, args.iters, msl=args.msl or None))
+            rows.append(bench_attention(nh, nkv, 128, kv, args.iters, msl=args.msl or None))
     if args.kernel in ("prefill_attention", "all"):
         lens = [int(v) for v in args.tokens.split(",")] if args.tokens else ([1024] if args.quick else [1024, 3202])
         for t in lens:
