@@ -110,7 +110,10 @@ def model_file(config: str, rank: int, world: int, dist, dtype: str = "fp16"):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region.  The sampler
+    starts before the region and the region starts only once its first sample has arrived
+    (nvidia-smi takes a few hundred ms to start); samples taken inside the region are kept, and the
+    first one after it when the region is shorter than the sampling period."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -118,26 +121,45 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.samples = []  # (monotonic time, line)
+        self.lines = []
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.samples.append((time.monotonic(), line))
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            t_wait = time.monotonic() + 5.0
+            while not self.samples and time.monotonic() < t_wait and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        self.t1 = time.monotonic()
         if self.proc:
+            t_wait = self.t1 + 0.6
+            while not any(t >= self.t0 for t, _ in self.samples) and time.monotonic() < t_wait:
+                time.sleep(0.01)
             self.proc.send_signal(signal.SIGTERM)
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.reader.join(timeout=2)
+            inside = [l for t, l in self.samples if self.t0 <= t <= self.t1]
+            after = [l for t, l in self.samples if t > self.t1]
+            self.lines = inside if inside else after[:1]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -359,6 +381,16 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms_dev = float(tt.item())
     value = args.steps / (ms_dev / 1000.0)
+    clocks = clk.summary()
+    if world > 1:
+        # every rank sampled its own GPU: the slowest median, all reasons, per-rank detail
+        per = [None] * world
+        dist.all_gather_object(per, clocks)
+        meds = [p["sm_mhz"] for p in per if p["sm_mhz"] is not None]
+        clocks = {"sm_mhz": min(meds) if meds else None,
+                  "sm_max_mhz": max((p["sm_max_mhz"] for p in per if p["sm_max_mhz"] is not None), default=None),
+                  "reasons": sorted(set().union(*(p["reasons"] for p in per))),
+                  "samples": sum(p["samples"] for p in per), "per_rank_sm_mhz": [p["sm_mhz"] for p in per]}
 
     # ---------------------------------------------------------------- end to end through the C ABI
     # (a) yb_forward_sample: the decode loop of yalm's main.cpp (forward + Sampler::sample at
@@ -535,7 +567,7 @@ def main():
             "tp_check": tp_check,
             "tp_exchange_us": tp_ex,
             "long_context": long_ctx,
-            "clocks": clk.summary(),
+            "clocks": clocks,
             "gpu_launches": launches_per_step * args.steps,
         }
         print(json.dumps(out))

@@ -46,3 +46,24 @@ def test_yalm_generation_stats_definition():
     """yalm's throughput (src/main.cpp:195-206): all tokens of the sequence over hydrate + decode."""
     s = bench.yalm_generation_stats(16, 120, 0.5, 0.01)
     assert s == {"tokens": 136, "hydrate_s": 0.5, "total_s": 1.7, "throughput_tok_s": 80.0}
+
+
+def test_clock_sampler_waits_for_its_first_sample_and_keeps_one_for_short_regions(tmp_path, monkeypatch):
+    """A fake nvidia-smi that starts slowly and prints a sample every 50 ms: the timed region opens
+    only after the first sample, and a region shorter than the sampling period still records the
+    first sample after it."""
+    import os
+    import time
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/sh\nsleep 0.3\nwhile true; do echo '0, 1965, 1965, 700.0, 0x0, Not Active, "
+                    "Not Active, Not Active, Not Active'; sleep 0.05; done\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+    t = time.monotonic()
+    with bench.ClockSampler(0) as c:
+        assert time.monotonic() - t >= 0.25  # waited for the sampler to start
+    s = c.summary()
+    assert s["samples"] >= 1 and s["sm_mhz"] == 1965.0 and s["reasons"] == []
+    with bench.ClockSampler(0) as c:
+        time.sleep(0.3)
+    assert c.summary()["samples"] >= 3
