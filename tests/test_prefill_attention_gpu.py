@@ -51,3 +51,28 @@ def test_prefill_attention_matches_reference(gpu, nh, nkv, hd, msl, T, pos0):
     # the outputs are stored as fp16: half an fp16 ulp of |ref| plus the fp32-path rounding
     err = np.abs(got - ref) - (2.0 ** -11 * np.abs(ref) + 2e-4)
     assert err.max() <= 0, float(np.abs(got - ref).max())
+
+
+@pytest.mark.parametrize("nh,nkv,hd,msl,T,pos0", [(32, 8, 128, 512, 77, 50), (8, 2, 64, 256, 33, 10)])
+def test_prefill_attention_ignores_slots_past_the_prompt(gpu, nh, nkv, hd, msl, T, pos0):
+    """Cache slots past the last query's position hold NaN (never-written cache memory may hold any
+    bits): the kernel stages whole key tiles, and the slots past the causal range must contribute
+    nothing — a zero probability times a NaN value would poison the row."""
+    import torch
+    rng = np.random.default_rng(11 * T + pos0)
+    q = rng.standard_normal((T, nh, hd)).astype(np.float32)
+    k = rng.standard_normal((nkv, msl, hd)).astype(np.float16)
+    v = rng.standard_normal((nkv, msl, hd)).astype(np.float16)
+    k[:, pos0 + T:] = np.nan
+    v[:, pos0 + T:] = np.nan
+    dq = torch.from_numpy(q).cuda()
+    dk = torch.from_numpy(k.view(np.int16)).cuda()
+    dv = torch.from_numpy(v.view(np.int16)).cuda()
+    out = torch.zeros(T * nh * hd, dtype=torch.int16, device="cuda")
+    _lib.call("yb_prefill_attention_dev", _ptr(out), _ptr(dq), _ptr(dk), _ptr(dv), T, pos0, nh, nkv, hd, msl, None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().view(np.float16).astype(np.float64).reshape(T, nh, hd)
+    assert np.isfinite(got).all()
+    ref = _reference(q, k, v, T, pos0, nh, nkv, hd)
+    err = np.abs(got - ref) - (2.0 ** -11 * np.abs(ref) + 2e-4)
+    assert err.max() <= 0, float(np.abs(got - ref).max())

@@ -24,7 +24,7 @@ NVCC_FLAGS = ARCH + [
     "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC,-O3", "-I" + os.path.join(ROOT, "include"),
 ]
-CU_SOURCES = ["gemv.cu", "attention.cu", "persistent.cu", "engine.cu", "capi.cu", "noalloc.cu", "sampler.cu", "loader.cu", "prefill_gemm.cu", "prefill.cu", "prefill_run.cu"]
+CU_SOURCES = ["gemv.cu", "attention.cu", "persistent.cu", "engine.cu", "capi.cu", "noalloc.cu", "sampler.cu", "loader.cu", "prefill_gemm.cu", "prefill.cu", "prefill_attn_tc.cu", "prefill_run.cu"]
 HEADERS = ["common.cuh", "gemv.cuh", "attention.cuh", "persistent.cuh", "launch.h", "engine.h", "loader.h", "prefill.cuh",
            "prefill_gemm.cuh", "sampler.cuh", "tmap.h"]
 

@@ -301,7 +301,7 @@ extern "C" int yb_prefill_attention_dev(uint16_t* out, const float* q, const uin
   if (!out || !q || !k_cache || !v_cache) return set_error(YB_E_INVALID, "null buffer");
   YB_CK(prefill_attention(q, reinterpret_cast<const __half*>(k_cache), reinterpret_cast<const __half*>(v_cache),
                           reinterpret_cast<__half*>(out), nullptr, T, pos0, n_heads, n_kv_heads, head_dim, max_seq_len,
-                          static_cast<cudaStream_t>(stream)));
+                          nullptr, static_cast<cudaStream_t>(stream)));
   return 0;
 }
 

@@ -4,6 +4,9 @@
 // (+ residual) -> RMSNorm rows -> gate/up GEMM (+ SwiGLU) -> w2 GEMM (+ residual).
 #include "prefill.cuh"
 
+#include <cstdlib>
+#include <cstring>
+
 #include <math.h>
 
 namespace yb {
@@ -338,9 +341,21 @@ const void* pick_pa(int gq) {
 
 cudaError_t prefill_attention(const float* q, const __half* k_cache, const __half* v_cache, __half* out, __half* out_lo,
                               int T, int pos0, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
-                              cudaStream_t s) {
+                              unsigned* status, cudaStream_t s) {
   if (T <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || pos0 + T > max_seq_len) return cudaErrorInvalidValue;
   const int gq = n_heads / n_kv_heads;
+  // 0: mma.sync kernel; 1: tcgen05 where supported (default); 2: tcgen05 with the V descriptor's
+  // byte offsets swapped (a layout check)
+  static const int mode = [] {
+    const char* v = std::getenv("YB_PREFILL_ATTN");
+    if (!v) return 1;
+    if (!std::strcmp(v, "mma")) return 0;
+    if (!std::strcmp(v, "tc-swap")) return 2;
+    return 1;
+  }();
+  if (mode && prefill_attention_tc_supported(head_dim, gq))
+    return prefill_attention_tc(q, k_cache, v_cache, out, out_lo, T, pos0, n_heads, n_kv_heads, max_seq_len, status,
+                                mode == 2 ? 1 : 0, s);
   const void* fn = head_dim == 128 ? pick_pa<128>(gq) : head_dim == 64 ? pick_pa<64>(gq) : nullptr;
   if (!fn) return cudaErrorInvalidValue;
   const size_t smem = (size_t)4 * kPaKeys * pa_row_bytes(head_dim);

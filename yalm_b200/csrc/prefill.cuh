@@ -22,9 +22,18 @@ cudaError_t prefill_qkv_post(const float* qkv, int T, int pos0, int q_rows, int 
 
 // Causal GQA attention of T queries at positions pos0 .. pos0 + T - 1 over cache slots
 // 0 .. pos0 + t (src/infer.cpp:218-250): out fp16 [T][n_heads * head_dim], and with out_lo non-null
-// each value's fp16 remainder there.
+// each value's fp16 remainder there.  head_dim 128 runs on tcgen05 (prefill_attn_tc.cu), head_dim
+// 64 on mma.sync; YB_PREFILL_ATTN=mma selects the mma.sync kernel for both.  status (optional)
+// records a bounded wait that ran out.
 cudaError_t prefill_attention(const float* q, const __half* k_cache, const __half* v_cache, __half* out, __half* out_lo,
                               int T, int pos0, int n_heads, int n_kv_heads, int head_dim, int max_seq_len,
-                              cudaStream_t s);
+                              unsigned* status, cudaStream_t s);
+
+// The tcgen05 kernel alone (head_dim 128, n_heads / n_kv_heads in 1, 2, 4, 8).  v_desc_order 0 is the
+// V operand's descriptor as the kernel uses it; 1 swaps its two byte offsets (a layout check).
+bool prefill_attention_tc_supported(int head_dim, int gq);
+cudaError_t prefill_attention_tc(const float* q, const __half* k_cache, const __half* v_cache, __half* out,
+                                 __half* out_lo, int T, int pos0, int n_heads, int n_kv_heads, int max_seq_len,
+                                 unsigned* status, int v_desc_order, cudaStream_t s);
 
 }  // namespace yb

@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "tmap.h"
+#include "umma.cuh"
 
 namespace yb {
 
@@ -33,55 +34,8 @@ constexpr int kTileBBytes = kPreBN * kPreBK * 2;  // 32 KB
 constexpr int kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = 2 * kPreBN;             // two fp32 accumulators of 128 lanes x 256 columns
 
-// 2-D TMA tile load (no multicast) completing on an mbarrier.
-
-// UMMA shared-memory descriptor, K-major, SWIZZLE_128B: start address, leading byte offset 16 (unused
-// for swizzled K-major), stride byte offset 1024 (8 rows of 128 bytes), version 1, layout 2.
-__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;
-  d |= (uint64_t)(1024u >> 4) << 32;
-  d |= (uint64_t)1u << 46;
-  d |= (uint64_t)2u << 61;
-  return d;
-}
-
 // Instruction descriptor: fp16 A and B, fp32 accumulator, both K-major, M 128, N 256.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kPreBN >> 3) << 17) | ((uint32_t)(kPreBM >> 4) << 24);
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_c, uint64_t da, uint64_t db, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
-      ::"r"(tmem_c), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrives on `bar` once every MMA this thread issued before has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-               ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive fp32 columns of this thread's tensor-memory lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
+constexpr uint32_t kIdesc = umma_idesc_f16(kPreBM, kPreBN, 0, 0);
 
 }  // namespace
 
@@ -247,7 +201,7 @@ __global__ void __launch_bounds__(kPreThreads, 1)
           const uint32_t sb = sa + kTileABytes;
 #pragma unroll
           for (int k = 0; k < kPreBK / 16; ++k)  // 16 fp16 = 32 bytes further along the swizzled row
-            umma_f16(acc, umma_desc_k_sw128(sa + k * 32), umma_desc_k_sw128(sb + k * 32), (kb | k) ? 1u : 0u);
+            umma_f16(acc, umma_desc_k_sw128(sa + k * 32), umma_desc_k_sw128(sb + k * 32), kIdesc, (kb | k) ? 1u : 0u);
           umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
         if (!ok) break;

@@ -87,7 +87,7 @@ static int prefill_batched(yb_engine* e, const int* tokens, int n, int pos0) {
     YB_CK(prefill_qkv_post(p.qkv, n, pos0, e->q_rows, e->kv_rows, c.head_dim, c.rotary_dim, c.max_seq_len, c.qkv_clip,
                            e->inv_freq, p.q, L.k_cache, L.v_cache, s));
     YB_CK(prefill_attention(p.q, L.k_cache, L.v_cache, p.att, p.att + (size_t)n * e->q_rows, n, pos0, e->nh, e->nkv,
-                            c.head_dim, c.max_seq_len, s));
+                            c.head_dim, c.max_seq_len, e->status_d, s));
     if ((rc = gemm(p.att, L.wo, n, c.dim, e->q_rows, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
     YB_CK(prefill_rmsnorm(p.x, L.rms_ffn, p.xn, p.xn + (size_t)n * c.dim, n, c.dim, c.norm_eps, s));
     if ((rc = gemm(p.xn, L.w13, n, 2 * e->hid, c.dim, kPreSwiGLU, nullptr, p.h, e->hid, s))) return rc;
