@@ -101,3 +101,35 @@ def test_fp8_engine_matches_reference_on_twin(gpu, fp8_pair, executor):
     assert m.status() == 0
     m.close()
     print("fp8 worst max-abs logit diff", worst, "greedy compared", n_sure)
+
+
+@pytest.mark.gpu
+def test_fp8_7b_shapes_match_reference_on_twin(gpu):
+    """The Mistral-7B architecture cut to 2 layers, fp8: every matvec shape `bench.py --dtype fp8`
+    runs (QKV 6144 x 4096 and wo 4096 x 4096 as two 2048-column chunks per row group, gate/up
+    28672 x 4096, w2 4096 x 14336 as seven chunks, the 32000-row classifier) against yalm's fp16 CPU
+    path on the fp16 twin, teacher-forced, with the north star's logit gate."""
+    import oracle
+    from yalm_b200 import InferenceState, Model, YALMData, synth
+    shape = synth.shape_with("mistral-7b", n_layers=2, dtype="fp8")
+    d = synth.scratch_dir(3 * synth.file_bytes(shape))
+    fp8 = synth.write_yalm(os.path.join(d, "yalm_mistral-7b_l2_fp8_seed0.yalm"), shape, seed=0)
+    twin = synth.expand_fp8_to_fp16(fp8, os.path.join(d, "yalm_mistral-7b_l2_fp8_seed0_twin16.yalm"))
+    m = Model(YALMData(fp8)).cuda(0)
+    ref = oracle.RefModel(twin)
+    s = InferenceState(m.config)
+    rng = np.random.default_rng(78)
+    toks = [int(t) for t in rng.integers(0, m.config.vocab_size, 20)]
+    worst = 0.0
+    for pos, tok in enumerate(toks):
+        m.forward(s, tok, pos)
+        got, exp = s.logits(), ref.forward(tok, pos, 1)
+        dmax = float(np.abs(got - exp).max())
+        worst = max(worst, dmax)
+        cos = float(got @ exp / (np.linalg.norm(got) * np.linalg.norm(exp)))
+        assert dmax <= LOGIT_MAX_ABS and cos >= LOGIT_COS, (pos, dmax, cos)
+        assert int(np.argmax(got)) == int(np.argmax(exp)) or np.sort(exp)[-1] - np.sort(exp)[-2] < 2e-3, pos
+    assert m.status() == 0
+    m.close()
+    ref.close()
+    print("fp8 7B-shape worst max-abs logit diff", worst)

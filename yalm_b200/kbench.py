@@ -31,10 +31,13 @@ def _p(t):
 
 
 def _copies(nbytes):
+    if _RESIDENT:
+        return 1
     return max(1, math.ceil(4 * L2_BYTES / nbytes))
 
 
 _WARM = 3
+_RESIDENT = False  # --resident: one copy of the operands, which stays in L2 when it fits
 
 
 _LAST_SPREAD: dict = {}
@@ -220,9 +223,12 @@ def main(argv=None):
     ap.add_argument("--heads", default="32,8", help="attention: n_heads,n_kv_heads (head_dim 128)")
     ap.add_argument("--tokens", default="", help="prefill_attention, prefill: comma-separated prompt lengths")
     ap.add_argument("--warm", type=int, default=3, help="untimed launches per case before the timed ones")
+    ap.add_argument("--resident", action="store_true",
+                    help="one copy of each operand (L2-resident when it fits) instead of rotating over > 4 x L2")
     args = ap.parse_args(argv)
-    global _WARM
+    global _WARM, _RESIDENT
     _WARM = args.warm
+    _RESIDENT = args.resident
     import torch
     torch.cuda.set_device(0)
     rows = []
