@@ -240,8 +240,11 @@ int yb_qkv_dev(float* q_out, uint16_t* k_cache, uint16_t* v_cache, const float* 
 
 /* Decode attention for all heads over cache slots [0, kv_len) of k_cache / v_cache
  * ([n_kv_heads][max_seq_len][head_dim] fp16): out (n_heads*head_dim) fp32.
- * scratch_dev: yb_attention_scratch_bytes(...) bytes of device memory, zero-filled before its
- * first use and left zero by every call. */
+ * scratch_dev: yb_attention_scratch_bytes(...) bytes of device memory (the cluster records of the
+ * merge over several clusters of a kv head, and the kv heads' counters), zero-filled before its
+ * first use and left zero by every call.  The first call per shape and device sets up its launch
+ * (kernel attributes, the cluster size from the device's occupancy): make it outside stream
+ * capture. */
 int yb_attention_dev(float* out, const float* q, const uint16_t* k_cache, const uint16_t* v_cache, int n_heads,
                      int n_kv_heads, int head_dim, int max_seq_len, int kv_len, void* scratch_dev, void* stream);
 size_t yb_attention_scratch_bytes(int n_heads, int n_kv_heads, int head_dim, int max_seq_len);

@@ -1,7 +1,7 @@
 // Decode attention without any device allocation by the library or the caller.
 //
-// yb_attention_dev needs a scratch buffer from the caller (slice partials and the merge counters of
-// the split-K attention kernel).  Some callers cannot provide one at call time: a plugin running
+// yb_attention_dev needs a scratch buffer from the caller (the cluster records and the merge
+// counters of the attention kernel, used where several clusters share a kv head).  Some callers cannot provide one at call time: a plugin running
 // inside another framework whose allocator owns all device memory, or a serving loop that forbids
 // device allocation after start-up so that latency and memory use stay fixed.  For them this file
 // keeps the scratch in a fixed-size array in the library's own device memory (allocated by the
@@ -16,7 +16,7 @@
 
 namespace {
 
-// Scratch for yb_attention_dev_noalloc: slice partials first, then the per-kv-head merge counters.
+// Scratch for yb_attention_dev_noalloc: cluster records first, then the per-kv-head merge counters.
 // Its size is YB_ATTENTION_NOALLOC_SCRATCH_BYTES (include/yalm_b200.h).
 constexpr size_t kNoAllocScratchBytes = YB_ATTENTION_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
