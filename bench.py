@@ -185,6 +185,20 @@ def bench_prompt(vocab_size: int):
     return [int(t) for t in rng.integers(0, vocab_size, PROMPT_LEN)]
 
 
+def host_cpu() -> dict:
+    """The host's CPU model and logical core count (from /proc/cpuinfo), for the CPU baseline record."""
+    model, n = None, 0
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    n += 1
+                    model = model or line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return {"cpu_model": model, "host_logical_cpus": n or os.cpu_count()}
+
+
 def cpu_baseline(path: str, context: int, n_decode: int, prompt):
     """yalm's own CPU decode path (oracle/_ref/ref_decode, built from the reference sources) on a
     bounded sample of the same workload — the same prompt, then n_decode greedy steps at positions
@@ -246,7 +260,7 @@ def run_reference(args):
                    "parallelism": "cpu (yalm -d cpu, OpenMP)"},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
-                         "sample": sample},
+                         "sample": sample, **host_cpu()},
         "greedy_ids": d["tokens"],
         "reference_gpu": ref_gpu,
         "gpu_launches": 0,
@@ -514,7 +528,7 @@ def main():
             cpu = {"value": round(len(st) / sum(st), 4), "unit": "tok/s", "cores": d["threads"], "kind": "reference",
                    "sample": f"{len(st)} greedy decode tokens of the full {args.config} model after the workload's "
                              f"{PROMPT_LEN}-token prompt, yalm -d cpu code path (oracle/_ref/ref_decode), "
-                             f"{d['threads']} OpenMP threads"}
+                             f"{d['threads']} OpenMP threads", **host_cpu()}
             ref_ids = [int(t) for t in d["tokens"]]
             n = min(len(ref_ids), len(greedy))
             greedy_match = {"steps": n, "match": greedy[:n] == ref_ids[:n], "engine": greedy[:n], "reference": ref_ids[:n],
