@@ -133,3 +133,18 @@ def test_fp8_7b_shapes_match_reference_on_twin(gpu):
     m.close()
     ref.close()
     print("fp8 7B-shape worst max-abs logit diff", worst)
+
+
+@pytest.mark.gpu
+def test_fp8_tensor_core_matvec_matches_reference_on_twin(gpu):
+    """The tensor-core fp8 matvec (YB_TUNE=fp8mma=1: weights re-laid at upload into 16-row groups,
+    mma.sync with x as fp16 value + remainder columns), off by default, run in a child process (the
+    tuning is read once per process) through the 7B-shape check above."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, YB_TUNE="fp8mma=1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu",
+                        os.path.abspath(__file__) + "::test_fp8_7b_shapes_match_reference_on_twin"],
+                       cwd=root, env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, (r.stdout[-3000:], r.stderr[-2000:])

@@ -188,6 +188,37 @@ static int upload_weights(yb_engine* e, const yb_weights* w) {
   }
   if ((rc = ld.finish())) return rc;
   e->upload_bytes = ld.bytes();
+  if (e->esz == 1 && e->tune.fp8_mma) {
+    // the tensor-core fp8 matvec reads 16-row groups (fp8_group_layout): re-lay each matrix into a
+    // new buffer and release the row-major one (the embedding table stays row-major for the step
+    // kernel; a classifier tied to it gets its own grouped copy)
+    auto regroup = [&](__half** p, size_t rows, size_t cols, bool release) -> int {
+      __half* nb = nullptr;
+      int r = dev_alloc(e, &nb, fp8_group_bytes((long long)rows, (int)cols));
+      if (r) return r;
+      YB_CK(fp8_group_layout(*p, nb, (long long)rows, (int)cols, nullptr));
+      YB_CK(cudaDeviceSynchronize());
+      if (release) {
+        for (size_t i = 0; i < e->allocs.size(); ++i)
+          if (e->allocs[i] == *p) {
+            e->allocs.erase(e->allocs.begin() + (long)i);
+            YB_CK(cudaFree(*p));
+            break;
+          }
+      }
+      *p = nb;
+      return 0;
+    };
+    for (int l = 0; l < c.n_layers; ++l) {
+      LayerBuffers& L = e->layers[l];
+      if ((rc = regroup(&L.wqkv, (size_t)e->q_rows + 2 * e->kv_rows, dim, true))) return rc;
+      if ((rc = regroup(&L.wo, dim, (size_t)e->q_rows, true))) return rc;
+      if ((rc = regroup(&L.w13, 2 * (size_t)e->hid, dim, true))) return rc;
+      if ((rc = regroup(&L.w2, dim, (size_t)e->hid, true))) return rc;
+    }
+    if ((rc = regroup(&e->wcls, (size_t)e->vocab_l, dim, e->wcls != e->emb))) return rc;
+    e->fp8_grouped = true;
+  }
   return 0;
 }
 
@@ -199,7 +230,9 @@ static const unsigned long long* tp_in(yb_engine* e, int pt) {
 
 // Matrix pointer `cols` weights into each row (a column panel), for either weight type.
 static const __half* wcols(const yb_engine* e, const __half* base, size_t cols) {
-  return reinterpret_cast<const __half*>(reinterpret_cast<const unsigned char*>(base) + cols * e->esz);
+  // grouped fp8 (fp8_group_layout): a panel starts `cols` 16-row columns, cols * 16 bytes, in
+  return reinterpret_cast<const __half*>(reinterpret_cast<const unsigned char*>(base) +
+                                         cols * (e->fp8_grouped ? 16 : e->esz));
 }
 
 static GemvArgs base_args(yb_engine* e) {

@@ -94,6 +94,7 @@ struct yb_engine {
   yb_config cfg{};
   int tp_rank = 0, tp_size = 1;
   int esz = 2;  // bytes per weight: 2 fp16, 1 fp8 E5M2 (device matrices hold that many bytes per element)
+  bool fp8_grouped = false;  // fp8 matrices (not the embedding) in the tensor-core matvec's grouped layout
   // local (this rank's) shapes
   int nh = 0, nkv = 0, q_rows = 0, kv_rows = 0, hid = 0, vocab_l = 0;
 

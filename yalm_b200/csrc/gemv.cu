@@ -11,8 +11,24 @@ namespace yb {
 // IN: 0 = x as given, 1 = RMS-normalised x, 2 = RMS-normalised x plus the tensor-parallel partial
 // sums of the previous row-parallel matvec (GemvArgs::tp_ll).  Only IN == 2 instances carry the
 // exchange-read code, so the others keep their registers for the stream loop.
-// WT: weight type, 0 = fp16, 1 = fp8 E5M2 (the top byte of an fp16).  A 16-byte chunk of a row holds
-// EPC = 8 or 16 weights; thread t owns the chunks t, t + NT, ... and the matching EPC values of x.
+// WT: weight type, 0 = fp16, 1 = fp8 E5M2 (the top byte of an fp16) on the CUDA cores, 2 = fp8 E5M2
+// on the tensor cores.  A 16-byte chunk of a row holds EPC = 8 or 16 weights; thread t owns the
+// chunks t, t + NT, ... and the matching EPC values of x for the input prologue.
+//
+// WT = 2 reads the matrix in the grouped layout fp8_group_layout writes at upload: 16-row groups,
+// each stored as [16-column chunk][row][16 bytes], so that a stage (a group's chunk of up to
+// kMmaCols columns) is one contiguous bulk copy and the 8 rows an ldmatrix reads are 128 consecutive
+// bytes (no bank conflicts).  Warp w takes the chunk's columns [w kMmaCols / NW, ...).  The input x
+// is staged in shared memory as fp16 value and remainder planes; per 16 columns one
+// mma.sync.m16n8k16 (fp32 accumulate) takes A = the 16 weight rows, whose e5m2 bytes become fp16
+// exactly by a byte permute, and B = x with column 0 its values and column 1 its remainders
+// (columns 2-7 zero).  The k order inside each 16 columns is permuted the same way in A and B (lane
+// c holds columns 4c .. 4c + 3, the 4 bytes one ldmatrix lane receives), which leaves every dot
+// product unchanged.  Products are exact (value + remainder carry ~22 bits of x); value and
+// remainder sums meet at the group's last chunk and go to the cross-warp reduction as the CUDA-core
+// path's do.
+constexpr int kMmaCols = 1024;  // fp8 columns (bytes) of a row per stage, WT = 2
+constexpr int kMmaRows = 16;    // rows per group (the mma's M), WT = 2
 template <int NW, int KPT, int RT, int EPI, int IN, int WT>
 __global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvArgs a) {
   constexpr bool NORM = IN >= 1;
@@ -27,15 +43,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvA
   pdl_trigger();
   if (threadIdx.x == 0) timeline_stamp(a.trace, a.trace_stride, 0);
 
-  const int T = (a.rows + RT - 1) / RT;  // stages over the whole matrix
+  constexpr bool MMA = WT == 2;
+  const int C = a.cols;
+  // units of RT rows: one stage each, or (tensor cores) NC column-chunk stages each
+  const int NC = MMA ? (C + kMmaCols - 1) / kMmaCols : 1;
+  const int T = (a.rows + RT - 1) / RT;
   const int G = gridDim.x;
   const int s_begin = (int)((long long)T * blockIdx.x / G);
   const int s_end = (int)((long long)T * (blockIdx.x + 1) / G);
-  const int n_st = s_end - s_begin;
+  const int n_units = s_end - s_begin;
+  const int n_st = n_units * NC;
   const int row_begin = s_begin * RT;
   const int NS = a.n_slots;
   const unsigned SB = a.stage_bytes;
-  const int C = a.cols;
   const unsigned row_bytes = (unsigned)C * (WT ? 1u : 2u);
 
   unsigned char* ring = smem;
@@ -43,6 +63,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvA
   float* scratch = red + a.red_floats;                    // NW floats for the norm reduction
   uint64_t* full = reinterpret_cast<uint64_t*>(scratch + 32);
   uint64_t* empty = full + NS;
+  // WT = 2: x as fp16 value and remainder planes, C each, 16-byte aligned after the barriers
+  __half* xs_hi = reinterpret_cast<__half*>((reinterpret_cast<uintptr_t>(empty + NS) + 15) & ~uintptr_t(15));
+  __half* xs_lo = xs_hi + C;
   __shared__ int s_abort;
 
   if (threadIdx.x == 0) {
@@ -63,7 +86,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvA
     const bool contiguous = (a.ldw == (long long)C);
     // Warm L2 with the stages just beyond the ring: weights are static, so this (like the ring
     // fill below) may run before the previous kernel of the step has finished.
-    if (contiguous && a.l2_prefetch_stages > 0) {
+    if (!MMA && contiguous && a.l2_prefetch_stages > 0) {
       int pf_end = min(n_st, NS + a.l2_prefetch_stages);
       for (int i = NS; i < pf_end; ++i) {
         int row0 = row_begin + i * RT;
@@ -80,16 +103,27 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvA
           break;
         }
       }
-      const int row0 = row_begin + i * RT;
-      const int nr = min(RT, a.rows - row0);
-      mbar_arrive_expect_tx(&full[slot], (unsigned)nr * row_bytes);
       unsigned char* dst = ring + (size_t)slot * SB;
-      if (contiguous) {
-        bulk_g2s(dst, wbase + (size_t)row0 * row_bytes, (unsigned)nr * row_bytes, &full[slot], pol);
+      if (MMA) {
+        // group s_begin + i / NC, column chunk i % NC: contiguous in the grouped layout (groups
+        // ldw * 16 bytes apart, 16-column chunks 256 bytes apart)
+        const int j = i % NC;
+        const int ccb = min(kMmaCols, C - j * kMmaCols);
+        const unsigned char* src =
+            wbase + (size_t)(s_begin + i / NC) * (size_t)a.ldw * kMmaRows + (size_t)j * kMmaCols * kMmaRows;
+        mbar_arrive_expect_tx(&full[slot], (unsigned)(kMmaRows * ccb));
+        bulk_g2s(dst, src, (unsigned)(kMmaRows * ccb), &full[slot], pol);
       } else {
-        for (int r = 0; r < nr; ++r)
-          bulk_g2s(dst + (size_t)r * row_bytes, wbase + (size_t)(row0 + r) * (size_t)a.ldw * (WT ? 1u : 2u), row_bytes,
-                   &full[slot], pol);
+        const int row0 = row_begin + i * RT;
+        const int nr = min(RT, a.rows - row0);
+        mbar_arrive_expect_tx(&full[slot], (unsigned)nr * row_bytes);
+        if (contiguous) {
+          bulk_g2s(dst, wbase + (size_t)row0 * row_bytes, (unsigned)nr * row_bytes, &full[slot], pol);
+        } else {
+          for (int r = 0; r < nr; ++r)
+            bulk_g2s(dst + (size_t)r * row_bytes, wbase + (size_t)(row0 + r) * (size_t)a.ldw * (WT ? 1u : 2u),
+                     row_bytes, &full[slot], pol);
+        }
       }
       issued = i + 1;
       if (EPI == kEpiQKV && a.kv_prefetch && a.step && i + 1 == min(NS, n_st)) {
@@ -261,6 +295,83 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvA
   }
 
   constexpr int LOG_RT = (RT == 1) ? 0 : (RT == 2) ? 1 : (RT == 4) ? 2 : 3;
+  if constexpr (MMA) {
+    static_assert(RT == kMmaRows, "the tensor-core path folds 16-row groups (the mma's M)");
+    // x -> fp16 value and remainder planes in shared memory (this thread's chunks)
+#pragma unroll
+    for (int k = 0; k < KPT; ++k) {
+      const int c = k * NT + t;
+      if (c < n_chunks) {
+        uint32_t hv[8], lv[8];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          split_f16x2(xr[k][v].x, xr[k][v].y, hv[2 * v], lv[2 * v]);
+          split_f16x2(xr[k][v].z, xr[k][v].w, hv[2 * v + 1], lv[2 * v + 1]);
+        }
+        uint4* ph = reinterpret_cast<uint4*>(xs_hi + (size_t)c * EPC);
+        uint4* pl = reinterpret_cast<uint4*>(xs_lo + (size_t)c * EPC);
+        ph[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        ph[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+        pl[0] = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        pl[1] = make_uint4(lv[4], lv[5], lv[6], lv[7]);
+      }
+    }
+    named_sync(1, NT);
+    // B: lanes 0-3 hold column 0 (values of x), lanes 4-7 column 1 (remainders); the rest is zero
+    const int g = lane >> 2, c4 = lane & 3;
+    const uint32_t xsrc = smem_u32(g == 0 ? xs_hi : xs_lo) + 8u * (uint32_t)c4;
+    constexpr int WCOLS = kMmaCols / NW;  // columns of a chunk per warp
+    float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int i = 0; i < n_st; ++i) {
+      const int slot = i % NS;
+      if (!mbar_wait(&full[slot], (i / NS) & 1, a.status)) {
+        s_abort = 1;
+        break;
+      }
+      if (*(volatile int*)&s_abort) break;
+      const int j = i % NC;
+      const int ccb = min(kMmaCols, C - j * kMmaCols);
+      const uint32_t st = smem_u32(ring + (size_t)slot * SB);
+#pragma unroll
+      for (int q = 0; q < WCOLS / 32; ++q) {
+        const int kb = warp * WCOLS + q * 32;  // 2 k-steps of 16 columns
+        if (kb < ccb) {
+          uint32_t r[4];
+          // matrix m = lane / 8: rows 8 (m & 1) .., k-step kb / 16 + (m >> 1); its row lane % 8
+          ldsm_x4(r, st + (uint32_t)((kb / 16 + (lane >> 4)) * 256 + (8 * ((lane >> 3) & 1) + (lane & 7)) * 16));
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (kb + 16 * h < ccb) {
+              uint32_t A[4];
+              A[0] = __byte_perm(r[2 * h], 0u, 0x1404u);      // row g, columns 4c, 4c + 1
+              A[1] = __byte_perm(r[2 * h + 1], 0u, 0x1404u);  // row g + 8
+              A[2] = __byte_perm(r[2 * h], 0u, 0x3424u);      // row g, columns 4c + 2, 4c + 3
+              A[3] = __byte_perm(r[2 * h + 1], 0u, 0x3424u);  // row g + 8
+              uint32_t b0 = 0u, b1 = 0u;
+              if (g < 2) {
+                const uint32_t xa = xsrc + 2u * (uint32_t)(j * kMmaCols + kb + 16 * h);
+                asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
+              }
+              mma_16816(d[h], A, b0, b1);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (j == NC - 1) {
+        // the group is complete: lanes c4 = 0 hold rows g and g + 8, value (column 0) and
+        // remainder (column 1) sums
+        const int u = i / NC;
+        if (c4 == 0) {
+          red[(u * RT + g) * NW + warp] = (d[0][0] + d[1][0]) + (d[0][1] + d[1][1]);
+          red[(u * RT + g + 8) * NW + warp] = (d[0][2] + d[1][2]) + (d[0][3] + d[1][3]);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) d[h][0] = d[h][1] = d[h][2] = d[h][3] = 0.f;
+      }
+    }
+  } else
   for (int i = 0; i < n_st; ++i) {
     const int slot = i % NS;
     if (!mbar_wait(&full[slot], (i / NS) & 1, a.status)) {
@@ -304,7 +415,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 2) yb_stream_matvec(const GemvA
   if (t == 0) timeline_stamp(a.trace, a.trace_stride, 3);
 
   // -------------------------------------------------------------------- epilogue
-  const int n_rows = min(n_st * RT, a.rows - row_begin);
+  const int n_rows = min(n_units * RT, a.rows - row_begin);
   if (EPI == kEpiStore || EPI == kEpiResid || EPI == kEpiResidTP || EPI == kEpiStoreTP) {
     for (int lr = t; lr < n_rows; lr += NT) {
       float s = 0.f;
@@ -461,11 +572,17 @@ const void* pick(int kpt, int rt, int epi, int in, int wt) {
       case 4: return pick1<4, 0>(rt, epi, in);
       case 7: return pick1<7, 0>(rt, epi, in);
     }
-  } else {
+  } else if (wt == 1) {
     switch (kpt) {
       case 1: return pick1<1, 1>(rt, epi, in);
       case 2: return pick1<2, 1>(rt, epi, in);
       case 4: return pick1<4, 1>(rt, epi, in);
+    }
+  } else if (rt == kMmaRows) {
+    switch (kpt) {
+      case 1: return pick2<1, kMmaRows, 2>(epi, in);
+      case 2: return pick2<2, kMmaRows, 2>(epi, in);
+      case 4: return pick2<4, kMmaRows, 2>(epi, in);
     }
   }
   return nullptr;
@@ -502,6 +619,7 @@ LaunchTuning LaunchTuning::from_env() {
         else if (k == "aslots" && v >= 16 && v % 16 == 0) t.attn_cta_slots = v;
         else if (k == "acslots" && v >= 16 && v % 16 == 0) t.attn_cluster_slots = v;
         else if (k == "acl" && v >= 0 && v <= 16) t.attn_cluster = v;
+        else if (k == "fp8mma" && v >= 0) t.fp8_mma = v != 0;
         else if (k == "acs" && v >= 0 && v <= 32) t.attn_clusters_per_head = v;
       }
       i = j + 1;
@@ -529,34 +647,72 @@ GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const Laun
   p.kpt = gemv_kpt_for(cols, esz);
   if (p.kpt < 0) return p;
   const int row_bytes = cols * esz;
+  // fp8 weights on the CUDA cores (WT = 1), or with YB_TUNE=fp8mma=1 on the tensor cores (WT = 2, the
+  // grouped layout the engine then writes at upload)
+  const int wt = esz == 2 ? 0 : (tune.fp8_mma ? 2 : 1);
   int rt = 1;
   while (rt < 8 && (rt * 2) * row_bytes <= tune.stage_bytes_target) rt *= 2;
   const bool pairs = (epi == kEpiGateUp || epi == kEpiQKV);
   if (pairs && rt < 2) rt = 2;
   if (pairs && (rows % 2) != 0) return p;
+  if (wt == 2) rt = kMmaRows;
   p.rt = rt;
+  p.wt = wt;
   const int T = (rows + rt - 1) / rt;
   const int max_grid = n_sms * tune.ctas_per_sm;
   p.grid = T < max_grid ? T : max_grid;
-  const int stages_per_cta = (T + p.grid - 1) / p.grid;
-  p.red_floats = stages_per_cta * rt * kGemvWarps;
-  p.stage_bytes = (unsigned)((rt * row_bytes + 127) / 128 * 128);
-  const int fixed = p.red_floats * 4 + 32 * 4 + 16 * 2 * 8 + 64;
+  const int units_per_cta = (T + p.grid - 1) / p.grid;
+  // tensor-core fp8: a stage is a group's chunk of up to kMmaCols columns; x waits in shared memory
+  // as two fp16 planes
+  const int chunk = cols < kMmaCols ? cols : kMmaCols;
+  const int nc = wt == 2 ? (cols + kMmaCols - 1) / kMmaCols : 1;
+  const int stages_per_cta = units_per_cta * nc;
+  const int xs_bytes = wt == 2 ? 4 * cols + 16 : 0;
+  p.red_floats = units_per_cta * rt * kGemvWarps;
+  p.stage_bytes = wt == 2 ? (unsigned)((rt * chunk + 127) / 128 * 128) : (unsigned)((rt * row_bytes + 127) / 128 * 128);
+  const int fixed = p.red_floats * 4 + 32 * 4 + 16 * 2 * 8 + 64 + xs_bytes;
   int ns = (tune.smem_budget - fixed) / (int)p.stage_bytes;
   if (ns > tune.max_slots) ns = tune.max_slots;
   if (ns > 16) ns = 16;
   if (ns > stages_per_cta) ns = stages_per_cta < 2 ? 2 : stages_per_cta;
   if (ns < 2) ns = 2;
   p.n_slots = ns;
-  p.smem = (size_t)ns * p.stage_bytes + (size_t)p.red_floats * 4 + 32 * 4 + (size_t)ns * 2 * 8;
+  p.smem = (size_t)ns * p.stage_bytes + (size_t)p.red_floats * 4 + 32 * 4 + (size_t)ns * 2 * 8 + (size_t)xs_bytes;
   if (tp_in && !norm) return p;
-  p.fn = pick(p.kpt, p.rt, epi, tp_in ? 2 : norm ? 1 : 0, esz == 1 ? 1 : 0);
+  p.fn = pick(p.kpt, p.rt, epi, tp_in ? 2 : norm ? 1 : 0, wt);
   p.norm = norm;
   p.ok = p.fn != nullptr && p.smem <= 226 * 1024;
   return p;
 }
 
 cudaError_t gemv_prepare(const GemvPlan& p) { return raise_smem_cap(p.fn); }
+
+// Grouped fp8 layout (WT = 2): dst 16-byte unit u = ((group * chunks + chunk) * 16 + row) holds
+// columns [16 chunk, 16 chunk + 16) of row 16 group + row of src (zeros past the last row).
+__global__ void fp8_group_layout_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, long long rows,
+                                        int cols) {
+  const long long chunks = cols / 16;
+  const long long units = (rows + kMmaRows - 1) / kMmaRows * kMmaRows * chunks;
+  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (long long)gridDim.x * blockDim.x) {
+    const long long r = u % kMmaRows, rest = u / kMmaRows;
+    const long long chunk = rest % chunks, group = rest / chunks;
+    const long long row = group * kMmaRows + r;
+    dst[u] = row < rows ? src[row * chunks + chunk] : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+size_t fp8_group_bytes(long long rows, int cols) {
+  return (size_t)((rows + kMmaRows - 1) / kMmaRows) * kMmaRows * (size_t)cols;
+}
+
+cudaError_t fp8_group_layout(const void* src, void* dst, long long rows, int cols, cudaStream_t stream) {
+  if (cols <= 0 || cols % 16 || rows <= 0 || (reinterpret_cast<uintptr_t>(src) & 15) ||
+      (reinterpret_cast<uintptr_t>(dst) & 15))
+    return cudaErrorInvalidValue;
+  fp8_group_layout_kernel<<<1184, 256, 0, stream>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst), rows,
+                                                     cols);
+  return cudaGetLastError();
+}
 
 cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages) {
   a.stage_bytes = p.stage_bytes;

@@ -26,10 +26,11 @@ struct LaunchTuning {
   int persist_claim_ctrs = 8;       // persistent executor: counters for the dynamically claimed rest
   int attn_cta_slots = 128;         // decode attention: cache slots per CTA before a kv head splits further
   int attn_cluster_slots = 1024;    // decode attention: slots per CTA of one cluster before a kv head takes more clusters
+  bool fp8_mma = false;             // fp8 weights: matvec on the tensor cores, grouped layout (measured slower)
   int attn_cluster = 0;             // decode attention: CTAs per cluster (0: chosen by attn_prepare)
   int attn_clusters_per_head = 0;   // decode attention: clusters per kv head (0: chosen by attn_prepare)
 
-  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2,aslots=128,acslots=1024,acl=0,acs=0"
+  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2,aslots=128,acslots=1024,acl=0,acs=0,fp8mma=0"
   // (read once per process) for tuning sweeps.
   static LaunchTuning from_env();
 };
@@ -38,6 +39,7 @@ struct GemvPlan {
   bool ok;
   const void* fn;
   int kpt, rt, grid, n_slots, red_floats;
+  int wt;  // weight mode of the kernel: 0 fp16, 1 fp8 on the CUDA cores, 2 fp8 on the tensor cores
   unsigned stage_bytes;
   size_t smem;
   bool norm;  // the kernel RMS-normalises x (GemvArgs::norm_w must then be set)
@@ -49,6 +51,12 @@ int gemv_kpt_for(int cols, int esz = 2);  // esz: weight bytes (2 fp16, 1 fp8 E5
 GemvPlan gemv_plan(int rows, int cols, int epi, bool norm, int n_sms, const LaunchTuning& tune, bool tp_in = false,
                    int esz = 2);
 cudaError_t gemv_prepare(const GemvPlan& p);  // once per plan, outside stream capture
+// fp8 matrices for the tensor-core matvec (GemvPlan::wt == 2): [rows][cols] row-major (cols a
+// multiple of 16) re-laid into 16-row groups of [16-column chunk][row][16 bytes], rows padded with
+// zeros to a multiple of 16; a column panel starting at column c of such a matrix begins c * 16
+// bytes in, groups cols * 16 bytes apart (GemvArgs::ldw = cols).
+size_t fp8_group_bytes(long long rows, int cols);
+cudaError_t fp8_group_layout(const void* src, void* dst, long long rows, int cols, cudaStream_t stream);
 cudaError_t gemv_launch(const GemvPlan& p, GemvArgs a, cudaStream_t stream, bool pdl, int l2_prefetch_stages);
 
 // Raises a kernel's dynamic shared-memory cap to everything the device allows next to the kernel's
