@@ -1,7 +1,7 @@
 """Isolated decode-kernel benchmark (benchmark config 4; the counterpart of yalm's
 `build/test -bk {matmul,matmul-wide,mha,ffn}`, src/test.cpp:339-405).
 
-    python -m yalm_b200.kbench [--kernel gemv|gateup|qkv|attention|prefill_attention|prefill|all]
+    python -m yalm_b200.kbench [--kernel gemv|gateup|qkv|attention|prefill_attention|prefill_gemm|prefill|all]
                                [--iters N] [--warm W] [--quick]
 
 Each launch goes through the C ABI (yb_gemv_dev, yb_gateup_dev, yb_qkv_dev, yb_attention_dev) on
@@ -156,6 +156,32 @@ def bench_attention(nh, nkv, hd, kv_len, iters, seed=0, msl=None):
             "max_active_clusters": list(info[4:20]), **_LAST_SPREAD}
 
 
+def bench_prefill_gemm(M, N, K, planes, swiglu, iters, seed=0):
+    """One batched-prefill GEMM (yb_prefill_gemm_dev): C[M][N] = A[M][K] . W[N][K]^T on tcgen05, A as
+    one fp16 plane or as the prefill's two (value, remainder: 2M rows, each product two MMAs); the
+    fp32 store epilogue, or with `swiglu` the gate/up form the prefill runs (SwiGLU of column pairs
+    to fp16, with the remainder plane written when A has two).  FLOP counts the useful 2 M N K."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = (torch.randn(planes * M, K, device="cuda", generator=g)).half()
+    b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    epi = (2 if swiglu else 0) | (4 if planes == 2 else 0) | (8 if swiglu and planes == 2 else 0)
+    if swiglu:
+        out = torch.empty(2 * M * (N // 2), dtype=torch.float16, device="cuda")
+        args = (None, _p(out), N // 2)
+    else:
+        out = torch.empty(M, N, device="cuda")
+        args = (_p(out), None, N)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def fn(i):
+        _lib.call("yb_prefill_gemm_dev", args[0], args[1], _p(a), _p(b), M, N, K, epi, args[2], stream)
+    ms = _time(fn, iters)
+    return {"kernel": "prefill_gemm", "M": M, "N": N, "K": K, "a_planes": planes,
+            "epilogue": "swiglu_f16" if swiglu else "store_f32", "us": round(ms * 1000, 2),
+            "tflops": round(2.0 * M * N * K / (ms / 1000) / 1e12, 1), **_LAST_SPREAD}
+
+
 def bench_prefill_attention(nh, nkv, hd, T, iters, seed=0):
     """Causal attention of a T-token prompt (yb_prefill_attention_dev); the caches fit in L2, as in
     the prefill where each layer's K/V were just written."""
@@ -215,7 +241,8 @@ def bench_prefill(tokens, iters, config="mistral-7b", seed=0):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", default="all",
-                    choices=["gemv", "gateup", "qkv", "attention", "prefill_attention", "prefill", "all"])
+                    choices=["gemv", "gateup", "qkv", "attention", "prefill_attention", "prefill_gemm", "prefill",
+                             "all"])
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--quick", action="store_true", help="one shape per kernel (for profiler captures)")
     ap.add_argument("--kv-lens", default="", help="attention: comma-separated kv_len values")
@@ -251,6 +278,12 @@ def main(argv=None):
         lens = [int(v) for v in args.tokens.split(",")] if args.tokens else ([1024] if args.quick else [1024, 3202])
         for t in lens:
             rows.append(bench_prefill_attention(32, 8, 128, t, max(3, args.iters // 20)))
+    if args.kernel == "prefill_gemm":
+        T = int(args.tokens.split(",")[0]) if args.tokens else 3202
+        for planes in (1, 2):
+            for M, N, K, sw in ((T, 6144, 4096, False), (T, 4096, 4096, False), (T, 28672, 4096, False),
+                                (T, 4096, 14336, False), (T, 28672, 4096, True)):
+                rows.append(bench_prefill_gemm(M, N, K, planes, sw, max(3, args.iters // 10)))
     if args.kernel == "prefill":  # not part of "all": it writes and loads the 14 GB 7B checkpoint
         lens = [int(v) for v in args.tokens.split(",")] if args.tokens else [3202, 1024]
         rows.extend(bench_prefill(lens, max(1, args.iters // 100)))
