@@ -620,6 +620,7 @@ LaunchTuning LaunchTuning::from_env() {
         else if (k == "acslots" && v >= 16 && v % 16 == 0) t.attn_cluster_slots = v;
         else if (k == "acl" && v >= 0 && v <= 16) t.attn_cluster = v;
         else if (k == "fp8mma" && v >= 0) t.fp8_mma = v != 0;
+        else if (k == "pfplanes" && v >= 0 && v <= 15) t.prefill_planes = v;
         else if (k == "acs" && v >= 0 && v <= 32) t.attn_clusters_per_head = v;
       }
       i = j + 1;

@@ -27,10 +27,14 @@ struct LaunchTuning {
   int attn_cta_slots = 128;         // decode attention: cache slots per CTA before a kv head splits further
   int attn_cluster_slots = 1024;    // decode attention: slots per CTA of one cluster before a kv head takes more clusters
   bool fp8_mma = false;             // fp8 weights: matvec on the tensor cores, grouped layout (measured slower)
+  // batched prefill: GEMMs that take the activations' fp16 remainder plane besides their values (bit 0
+  // QKV, 1 wo, 2 gate/up, 3 w2).  Measured (7B, 3202-token prompt): all four 94.5 ms, worst logit
+  // 0.0072 against yalm's CPU path; QKV + wo (the default) 62.9 ms, 0.0107; the gate is 2e-2.
+  int prefill_planes = 3;
   int attn_cluster = 0;             // decode attention: CTAs per cluster (0: chosen by attn_prepare)
   int attn_clusters_per_head = 0;   // decode attention: clusters per kv head (0: chosen by attn_prepare)
 
-  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2,aslots=128,acslots=1024,acl=0,acs=0,fp8mma=0"
+  // Defaults, overridable with YB_TUNE="stage=16384,budget=100000,slots=8,l2pf=4,l2wo=2,l2qkv=4,ctas=2,aslots=128,acslots=1024,acl=0,acs=0,fp8mma=0,pfplanes=3"
   // (read once per process) for tuning sweeps.
   static LaunchTuning from_env();
 };

@@ -42,8 +42,10 @@ int ensure_buffers(yb_engine* e, int T) {
   return 0;
 }
 
-int gemm(const __half* A, const __half* B, int M, int N, int K, int epi, float* of, __half* oh, int ldo,
-         cudaStream_t s) {
+// planes: 2 = A as values + remainders ([2][M][K]), 1 = values only; lo_out: fp16 outputs also
+// write their remainder plane (for a two-plane GEMM after this one)
+int gemm(const __half* A, const __half* B, int M, int N, int K, int epi, float* of, __half* oh, int ldo, int planes,
+         bool lo_out, cudaStream_t s) {
   PrefillGemmArgs g{};
   g.M = M;
   g.N = N;
@@ -53,8 +55,8 @@ int gemm(const __half* A, const __half* B, int M, int N, int K, int epi, float* 
   g.out_f32 = of;
   g.out_f16 = oh;
   g.status = nullptr;
-  g.a_planes = 2;          // A: values + remainders, [2][M][K]
-  g.lo_out = oh ? 1 : 0;   // fp16 outputs feed the next GEMM as two planes too
+  g.a_planes = planes;
+  g.lo_out = oh && lo_out ? 1 : 0;
   YB_CK(prefill_gemm(A, B, g, s));
   return 0;
 }
@@ -80,18 +82,23 @@ static int prefill_batched(yb_engine* e, const int* tokens, int n, int pos0) {
   YB_CK(cudaMemcpyAsync(p.tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
   prefill_embed_kernel<<<n, 256, 0, s>>>(e->emb, p.tokens, p.x, c.dim);
   YB_CK(cudaGetLastError());
+  // which GEMMs take the remainder plane (bit 0 QKV, 1 wo, 2 gate/up, 3 w2)
+  const int pm = e->tune.prefill_planes;
+  auto planes = [pm](int bit) { return (pm >> bit) & 1 ? 2 : 1; };
   for (int l = 0; l < c.n_layers; ++l) {
     LayerBuffers& L = e->layers[l];
     YB_CK(prefill_rmsnorm(p.x, L.rms_att, p.xn, p.xn + (size_t)n * c.dim, n, c.dim, c.norm_eps, s));
-    if ((rc = gemm(p.xn, L.wqkv, n, qkv_rows, c.dim, kPreStore, p.qkv, nullptr, qkv_rows, s))) return rc;
+    if ((rc = gemm(p.xn, L.wqkv, n, qkv_rows, c.dim, kPreStore, p.qkv, nullptr, qkv_rows, planes(0), false, s)))
+      return rc;
     YB_CK(prefill_qkv_post(p.qkv, n, pos0, e->q_rows, e->kv_rows, c.head_dim, c.rotary_dim, c.max_seq_len, c.qkv_clip,
                            e->inv_freq, p.q, L.k_cache, L.v_cache, s));
     YB_CK(prefill_attention(p.q, L.k_cache, L.v_cache, p.att, p.att + (size_t)n * e->q_rows, n, pos0, e->nh, e->nkv,
                             c.head_dim, c.max_seq_len, e->status_d, s));
-    if ((rc = gemm(p.att, L.wo, n, c.dim, e->q_rows, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
+    if ((rc = gemm(p.att, L.wo, n, c.dim, e->q_rows, kPreAdd, p.x, nullptr, c.dim, planes(1), false, s))) return rc;
     YB_CK(prefill_rmsnorm(p.x, L.rms_ffn, p.xn, p.xn + (size_t)n * c.dim, n, c.dim, c.norm_eps, s));
-    if ((rc = gemm(p.xn, L.w13, n, 2 * e->hid, c.dim, kPreSwiGLU, nullptr, p.h, e->hid, s))) return rc;
-    if ((rc = gemm(p.h, L.w2, n, c.dim, e->hid, kPreAdd, p.x, nullptr, c.dim, s))) return rc;
+    if ((rc = gemm(p.xn, L.w13, n, 2 * e->hid, c.dim, kPreSwiGLU, nullptr, p.h, e->hid, planes(2), planes(3) == 2, s)))
+      return rc;
+    if ((rc = gemm(p.h, L.w2, n, c.dim, e->hid, kPreAdd, p.x, nullptr, c.dim, planes(3), false, s))) return rc;
   }
   return 0;
 }
