@@ -225,7 +225,9 @@ def test_kv_append_indexing_integer_coded(gpu, pos, msl):
     (32, 8, 128, 4096, 1), (32, 8, 128, 4096, 65), (32, 8, 128, 4096, 129), (32, 8, 128, 4096, 3232),
     (32, 8, 128, 4096, 4096), (64, 8, 128, 8192, 1152), (16, 16, 128, 512, 300), (16, 8, 64, 512, 511),
     (32, 8, 128, 32768, 16384), (32, 8, 128, 32768, 32768), (8, 2, 128, 8192, 8192), (4, 1, 128, 16384, 16000),
-    (8, 1, 64, 4096, 2049), (64, 8, 128, 8192, 8192), (4, 1, 128, 32768, 30000), (8, 2, 128, 32768, 32768)])
+    (8, 1, 64, 4096, 2049), (64, 8, 128, 8192, 8192), (4, 1, 128, 32768, 30000), (8, 2, 128, 32768, 32768),
+    # one tensor-parallel rank's share of the 7B shape (2, 4, 8 ranks) at the scaling bench's kv_len
+    (16, 4, 128, 4096, 100), (8, 2, 128, 4096, 136), (4, 1, 128, 4096, 17), (4, 1, 128, 4096, 129)])
 def test_attention_matches_oracle(gpu, nh, nkv, hd, msl, kv_len):
     """Includes config 4's long caches (kv_len 16384 and 32768 at max_seq_len 32768: over 3000 slots
     per CTA of a 10-CTA cluster on a B200) and long caches of one or two kv heads, which several
